@@ -1,0 +1,212 @@
+/*
+ * frag.h — C ABI of libfrag.so, the B200 (sm_100a) kernels for the memory-bound
+ * Llama training-graph fragments collected in SherlockNoMad/KernelProblems.
+ *
+ * The reference exposes each fragment as a Python `kernel_function(*inputs)`
+ * (a drop-in for the fragment's torch `Model.forward`).  These entry points are
+ * what such a function binds to: plain device pointers, element counts and
+ * strides, a CUDA stream, and an integer status.  No torch types cross this
+ * boundary.
+ *
+ * Conventions shared by every entry point
+ *   - bf16 tensors are passed as `const void*` / `void*` holding IEEE bfloat16
+ *     bit patterns; fp32 tensors as `float*`; indices as int64 unless stated.
+ *   - Row-major, innermost dimension contiguous.  Fast paths need 16-byte
+ *     aligned base pointers and a row size that is a multiple of 8 bf16
+ *     elements; other shapes run a slower generic kernel, never a CPU path.
+ *   - Every call is asynchronous on `stream` (the caller's current stream) and
+ *     never synchronises.  Inputs are read-only; outputs are caller-owned.
+ *   - Return value: FRAG_OK (0) or one of the frag_status codes below.  Shape
+ *     and pointer checks happen on the host before any launch; a failed launch
+ *     returns FRAG_ERR_CUDA and frag_last_cuda_error() gives the cudaError_t.
+ *   - Device-detected input errors (an index outside the table) are written to
+ *     the optional `status` word (device memory, int32) with atomicOr of the
+ *     FRAG_DEVFLAG_* bits; the call itself still returns FRAG_OK because the
+ *     host cannot see device data without synchronising.
+ *   - Entry points that need scratch memory take a caller-provided workspace
+ *     and expose a *_workspace_bytes() size query; nothing here allocates.
+ */
+#ifndef FRAG_H_
+#define FRAG_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FRAG_API __attribute__((visibility("default")))
+#else
+#define FRAG_API
+#endif
+
+typedef struct CUstream_st* frag_stream_t; /* == cudaStream_t */
+
+enum frag_status {
+  FRAG_OK = 0,
+  FRAG_ERR_INVALID_ARG = 1, /* null pointer where one is required, negative size */
+  FRAG_ERR_SHAPE = 2,       /* shape not supported by any kernel variant        */
+  FRAG_ERR_ALIGN = 3,       /* misaligned pointer or stride                      */
+  FRAG_ERR_WORKSPACE = 4,   /* workspace missing or smaller than the query says  */
+  FRAG_ERR_CUDA = 5,        /* a CUDA runtime call or launch failed              */
+  FRAG_ERR_NO_DEVICE = 6    /* no CUDA device is visible                         */
+};
+
+/* Bits written into a caller's device status word by kernels. */
+enum frag_devflag {
+  FRAG_DEVFLAG_INDEX_OOB = 1 /* an embedding id was outside [0, vocab_total)     */
+};
+
+/* RoPE layouts.  NEOX pairs element i with i + D/2 (rotate-half);
+ * INTERLEAVED pairs 2i with 2i+1 (complex view, the reference's layout). */
+enum frag_rope_layout { FRAG_ROPE_NEOX = 0, FRAG_ROPE_INTERLEAVED = 1 };
+
+/* Position tensor dtypes for RoPE. NONE means position = token index s. */
+enum frag_pos_dtype { FRAG_POS_NONE = 0, FRAG_POS_I32 = 1, FRAG_POS_I64 = 2 };
+
+FRAG_API const char* frag_version(void);
+FRAG_API const char* frag_status_string(int status);
+/* cudaError_t of the most recent FRAG_ERR_CUDA on this host thread. */
+FRAG_API int frag_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------- *
+ * RMSNorm forward with saved rstd.
+ *   rstd[m] = 1 / sqrt(mean_n(x[m,n]^2) + eps)            (fp32 accumulation)
+ *   y[m,n]  = bf16((x[m,n] * rstd[m]) * w[n])
+ * Replaces aten._fused_rms_norm as called by
+ *   v8/f4e9e58fef73/problem.py:28 (y + rstd) and its Triton drop-in
+ *   v8/f4e9e58fef73/optimized_kernel.py:43 `kernel_function(add_recomputed, weight)`,
+ *   v8/4b90e2d83144/optimized_kernel.py:30 `kernel_function(embedding, weight, eps)`.
+ * x, y: bf16 [M,N]; w: bf16 [N]; rstd: fp32 [M] or NULL.
+ * ------------------------------------------------------------------------- */
+FRAG_API int frag_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd,
+                     int64_t M, int64_t N, float eps, frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Residual add + RMSNorm forward.
+ *   h = bf16(res + x);  rstd, y as frag_rmsnorm_fwd applied to h.
+ * Replaces aten.add -> aten._fused_rms_norm of
+ *   v8/7884328a5557/problem.py:20,23 and its drop-in
+ *   v8/7884328a5557/optimized_kernel.py:37 `kernel_function(mm_220, add_61, w)`.
+ * res, x, h, y: bf16 [M,N]; h and rstd may be NULL (not written).
+ * ------------------------------------------------------------------------- */
+FRAG_API int frag_add_rmsnorm_fwd(const void* res, const void* x, const void* w, void* h,
+                         void* y, float* rstd, int64_t M, int64_t N, float eps,
+                         frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * RMSNorm backward (dx and a deterministic column-reduced dweight), with the
+ * optional residual-stream adds of the fused backward fragments.
+ *   dy      = dy2 ? bf16(dy + dy2) : dy
+ *   rstd    = rstd ? rstd : 1/sqrt(mean(x^2) + eps)          (recompute)
+ *   xhat    = x * rstd;  gw = dy * w
+ *   dx      = (gw - xhat * mean_n(xhat * gw)) * rstd
+ *   dx_out  = dres ? bf16(dres + bf16(dx)) : bf16(dx)
+ *   dw[n]   = sum_m dy[m,n] * xhat[m,n]      fp32, fixed summation order
+ * Replaces aten._fused_rms_norm_backward as called by
+ *   v7/45990c83cfd6/problem.py:23 (recompute + bwd; drop-in
+ *     v7/45990c83cfd6/optimized_kernel.py:96 `kernel_function(x, weight, grad_out, eps)`),
+ *   v7/7f544ceb2120/problem.py:23-38 (add -> bwd -> add -> fp32; drop-in
+ *     v7/7f544ceb2120/optimized_kernel.py:71),
+ *   v8/d8f596b3df34/problem.py:23-40 (drop-in v8/d8f596b3df34/optimized_kernel.py:64).
+ * dx_out: bf16 [M,N]; dw: fp32 [N] or NULL; dw_bf16: bf16 [N] or NULL.
+ * workspace: frag_rmsnorm_bwd_workspace_bytes(M, N) bytes of device memory.
+ * The sum over rows is split into fixed row blocks whose fp32 partials are
+ * added in block order, so dw is bitwise reproducible for a given M, N and GPU.
+ * ------------------------------------------------------------------------- */
+FRAG_API size_t frag_rmsnorm_bwd_workspace_bytes(int64_t M, int64_t N);
+FRAG_API int frag_rmsnorm_bwd(const void* dy, const void* dy2, const void* x,
+                     const float* rstd, const void* w, const void* dres,
+                     void* dx_out, float* dw, void* dw_bf16, int64_t M,
+                     int64_t N, float eps, void* workspace,
+                     size_t workspace_bytes, frag_stream_t stream);
+
+/* Row-block count G of frag_rmsnorm_bwd for 16-byte aligned operands.  After
+ * a frag_rmsnorm_bwd call the first G*N floats of its workspace hold the
+ * per-block dweight partials [G, N] (whether or not dw was requested), which
+ * multi-GPU callers may reduce across ranks themselves. */
+FRAG_API int64_t frag_rmsnorm_bwd_num_blocks(int64_t M, int64_t N);
+/* Sum partials[G, N] over G in order into dw (fp32) and/or dw_bf16. */
+FRAG_API int frag_dw_reduce(const float* partials, int64_t G, int64_t N, float* dw,
+                   void* dw_bf16, frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Token-embedding gather (optionally one vocab shard of a vocab-parallel table).
+ *   v = ids[t] - vocab_lo
+ *   out[t,:] = (0 <= v < shard_rows) ? table[v,:] : 0
+ * ids outside [0, vocab_total) also produce a zero row and set
+ * FRAG_DEVFLAG_INDEX_OOB in *status (if status is not NULL).
+ * Replaces aten.embedding of v7/1e49beb8a123/problem.py:20-23 (drop-in
+ * v7/1e49beb8a123/optimized_kernel.py:34 `kernel_function(wait_tensor_871, ids)`).
+ * ids: int64 [T]; table: bf16 [shard_rows, D]; out: bf16 [T, D].  Bit exact.
+ * ------------------------------------------------------------------------- */
+FRAG_API int frag_embedding_fwd(const int64_t* ids, const void* table, void* out,
+                       int64_t T, int64_t shard_rows, int64_t D,
+                       int64_t vocab_lo, int64_t vocab_total, int32_t* status,
+                       frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Token-embedding backward into an fp32 table gradient (deterministic).
+ *   G[v,:] = sum over t in increasing order with ids[t]-vocab_lo == v and
+ *            ids[t] != padding_idx of grad[t,:]      (fp32 accumulation)
+ * Every row of G in [0, shard_rows) is written exactly once (zero rows
+ * included), so G needs no prior memset.
+ * Replaces aten.embedding_dense_backward -> _to_copy(fp32) of
+ *   v7/a12a160cb11b/problem.py:16,19 (drop-in
+ *   v7/a12a160cb11b/optimized_kernel.py:37 `kernel_function(add_223, ids)`),
+ * whose Triton version accumulates with fp32 atomics (not reproducible).
+ * ids: int64 [T]; grad: bf16 [T, D]; G: fp32 [shard_rows, D].
+ * padding_idx < 0 disables padding.  workspace: *_workspace_bytes(T, shard_rows).
+ * ------------------------------------------------------------------------- */
+FRAG_API size_t frag_embedding_bwd_workspace_bytes(int64_t T, int64_t shard_rows);
+FRAG_API int frag_embedding_bwd(const int64_t* ids, const void* grad, float* G,
+                       int64_t T, int64_t shard_rows, int64_t D,
+                       int64_t vocab_lo, int64_t vocab_total,
+                       int64_t padding_idx, void* workspace,
+                       size_t workspace_bytes, int32_t* status,
+                       frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Rotary position embedding on up to two tensors (q and k) in one launch.
+ * Tensor i (i = 0, 1) is bf16 [B, S, H_i, D] addressed by element strides
+ * (stride_b, stride_s, stride_h; the last dimension is contiguous), and is
+ * written to out_i with its own strides.  in and out may alias exactly.
+ * Angle for pair j (0 <= j < D/2) at position p:
+ *   freqs == NULL : theta_j = p * inv_freq[j], inv_freq[j] = theta^(-2j/D)
+ *                   (fp32, cos/sin evaluated in registers; nothing is read
+ *                   from HBM besides x and the positions)
+ *   freqs != NULL : (cos, sin) := (re, im) of freqs[p, j], a complex64 table
+ *                   of row stride freqs_stride (in complex elements) — the
+ *                   reference's freqs_cis input (not necessarily unit modulus).
+ * layout NEOX rotates (x_j, x_{j+D/2}); INTERLEAVED rotates (x_2j, x_2j+1).
+ * inverse != 0 rotates by the conjugate (the backward of RoPE).
+ * Positions p = pos[b*pos_stride_b + s*pos_stride_s] (int32 or int64), or s.
+ * Replaces the complex-mul RoPE of v8/c8c60d8f7015/problem.py:18-70 (drop-in
+ * v8/c8c60d8f7015/optimized_kernel.py:48), v8/97032595d968 (:44),
+ * v8/e29b92927600 (:54), v8/493cad38cac9 (:48), and the backward fragments
+ * v7/bfe872e373e4 (:54), v7/5c65f62b0422 (:45), v6/03d64c25b654 (:51).
+ * ------------------------------------------------------------------------- */
+typedef struct frag_rope_tensor {
+  const void* x;
+  void* out;
+  int64_t H;
+  int64_t x_stride_b, x_stride_s, x_stride_h;
+  int64_t out_stride_b, out_stride_s, out_stride_h;
+} frag_rope_tensor;
+
+FRAG_API int frag_rope(const frag_rope_tensor* tensors, int num_tensors, int64_t B,
+              int64_t S, int64_t D, const void* pos, int pos_dtype,
+              int64_t pos_stride_b, int64_t pos_stride_s, const float* freqs,
+              int64_t freqs_stride, float theta, int layout, int inverse,
+              frag_stream_t stream);
+
+/* Device properties the host layer uses to size launches and workspaces. */
+FRAG_API int frag_device_sm_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FRAG_H_ */

@@ -1,0 +1,168 @@
+// common.cuh — helpers shared by the libfrag.so kernels (sm_100a).
+//
+// bf16 values travel as raw 16-bit patterns packed in uint32/uint4 words so
+// every global access is a 128-bit vector op.  Widening bf16 -> fp32 is a
+// shift; narrowing uses the hardware round-to-nearest-even conversion.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "frag.h"
+
+namespace frag {
+
+// ---------------------------------------------------------------- host side
+
+// Per-thread record of the last CUDA error seen by an entry point.
+void set_last_cuda_error(cudaError_t e);
+
+// Returns FRAG_OK, or FRAG_ERR_CUDA after recording the error.
+inline int check_launch() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return FRAG_ERR_CUDA;
+  }
+  return FRAG_OK;
+}
+
+inline int cuda_status(cudaError_t e) {
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return FRAG_ERR_CUDA;
+  }
+  return FRAG_OK;
+}
+
+inline bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// Number of SMs on the current device (cached per device).
+int sm_count();
+// Current device ordinal or -1.
+int current_device();
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ---------------------------------------------------------------- device side
+
+__device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ float bf16_to_f(uint16_t u) {
+  return __uint_as_float(static_cast<uint32_t>(u) << 16);
+}
+
+// Two fp32 -> packed bf16x2 (lo in the low half), round to nearest even.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint16_t f_to_bf16(float f) {
+  __nv_bfloat16 v = __float2bfloat16_rn(f);
+  return *reinterpret_cast<uint16_t*>(&v);
+}
+// Round an fp32 value to the nearest bf16 and widen it back.
+__device__ __forceinline__ float round_bf16(float f) {
+  return bf16_to_f(f_to_bf16(f));
+}
+
+// 8 bf16 <-> 8 fp32
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  f[0] = bf16lo(v.x); f[1] = bf16hi(v.x);
+  f[2] = bf16lo(v.y); f[3] = bf16hi(v.y);
+  f[4] = bf16lo(v.z); f[5] = bf16hi(v.z);
+  f[6] = bf16lo(v.w); f[7] = bf16hi(v.w);
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 v;
+  v.x = pack_bf16x2(f[0], f[1]);
+  v.y = pack_bf16x2(f[2], f[3]);
+  v.z = pack_bf16x2(f[4], f[5]);
+  v.w = pack_bf16x2(f[6], f[7]);
+  return v;
+}
+
+// Streaming 128-bit load: read-only, not kept in L1 (each byte is read once).
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+// Cached 128-bit read-only load (data shared by many CTAs: weights, tables).
+__device__ __forceinline__ uint4 ld_cached(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ float4 ld_stream_f4(const void* p) {
+  float4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+// Plain 128-bit store (result is consumed by the next op, keep default policy).
+__device__ __forceinline__ void st_global(void* p, const uint4& v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
+// Streaming 128-bit store (evict-first: large outputs nobody re-reads soon).
+__device__ __forceinline__ void st_stream(void* p, const uint4& v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void st_stream_f4(void* p, const float4& v) {
+  asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float2 warp_sum2(float2 v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
+    v.y += __shfl_xor_sync(0xffffffffu, v.y, o);
+  }
+  return v;
+}
+
+// Block-wide sum in a fixed order (warp butterflies, then warps 0..nw-1 in
+// order), result broadcast to every thread.  `slots` is a [2][32] shared
+// array; `parity` alternates between consecutive calls so only one barrier
+// per call is needed (a warp cannot overwrite a slot another warp still reads:
+// it must first pass the barrier of the call in between).
+__device__ __forceinline__ float2 block_sum2(float2 v, float2 (*slots)[32], int parity) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = warp_sum2(v);
+  if (lane == 0) slots[parity][warp] = v;
+  __syncthreads();
+  float2 t = make_float2(0.f, 0.f);
+  for (int i = 0; i < nw; ++i) {
+    float2 s = slots[parity][i];
+    t.x += s.x;
+    t.y += s.y;
+  }
+  return t;
+}
+__device__ __forceinline__ float block_sum(float v, float (*slots)[32], int parity) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  if (lane == 0) slots[parity][warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += slots[parity][i];
+  return t;
+}
+
+}  // namespace frag

@@ -1,0 +1,570 @@
+// rmsnorm.cu — RMSNorm forward / residual-add + RMSNorm forward / RMSNorm
+// backward with a deterministic two-pass dweight, for bf16 rows on sm_100a.
+//
+// Math follows the fragments' torch reference path:
+//   forward  aten._fused_rms_norm   (v8/f4e9e58fef73/problem.py:28)
+//            rstd = 1/sqrt(mean(x^2) + eps), y = bf16((x * rstd) * w), fp32 math
+//   add      aten.add.Tensor in bf16 (v8/7884328a5557/problem.py:20): h = bf16(res + x)
+//   backward torch._decomp _fused_rms_norm_backward (torch 2.11,
+//            torch/_decomp/decompositions.py:1862-1933), called by
+//            v7/45990c83cfd6/problem.py:23 and v7/7f544ceb2120/problem.py:23-38:
+//            xhat = x*rstd, gw = dy*w,
+//            dx = (gw - xhat/N * sum(xhat*gw)) * rstd, dw = sum_rows(dy*xhat)
+//   The fused backward fragments round the grad sum and dx to bf16 before the
+//   residual add (v7/7f544ceb2120/problem.py:23-32), and so do we.
+//
+// Vector path (N % 8 == 0, 16-byte aligned pointers, N <= 16384): the row is
+// held in registers — thread t owns 16-byte chunks t, t+T, ..., so every load
+// instruction of a block is one fully coalesced span — and each element is
+// read from HBM exactly once.  Generic path: any N, two passes over the row.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace frag {
+namespace {
+
+struct RowCfg {
+  int vpt;      // 16-byte chunks per thread (0 = generic kernel)
+  int threads;  // block size, multiple of 32
+};
+
+RowCfg pick_row_cfg(int64_t N, bool aligned) {
+  // Register-resident rows: at most 512 threads x 4 chunks (N <= 16384), so
+  // every thread keeps <= 128 registers without spilling.
+  if (!aligned || N % 8 != 0 || N > 16384) return {0, 256};
+  const int64_t chunks = N / 8;
+  const int vpts[2] = {2, 4};
+  for (int vpt : vpts) {
+    int64_t t = (chunks + vpt - 1) / vpt;
+    t = (t + 31) / 32 * 32;
+    if (t <= 512) return {vpt, static_cast<int>(t)};
+  }
+  return {0, 256};
+}
+
+// ------------------------------------------------------------------ forward
+
+template <int VPT, bool HAS_RES, bool WRITE_H, bool WRITE_RSTD>
+__global__ void __launch_bounds__(512)
+rmsnorm_fwd_vec(const uint16_t* __restrict__ x, const uint16_t* __restrict__ res,
+                const uint16_t* __restrict__ w, uint16_t* __restrict__ h,
+                uint16_t* __restrict__ y, float* __restrict__ rstd, int N, float eps) {
+  __shared__ float slots[2][32];
+  const int chunks = N >> 3;
+  const int64_t row = blockIdx.x;
+  const size_t base = static_cast<size_t>(row) * N;
+
+  uint4 xv[VPT], rv[VPT], wv[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < chunks) {
+      xv[k] = ld_stream(x + base + c * 8);
+      if (HAS_RES) rv[k] = ld_stream(res + base + c * 8);
+      wv[k] = ld_cached(w + c * 8);
+    } else {
+      xv[k] = rv[k] = wv[k] = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    unpack8(xv[k], v[k]);
+    if (HAS_RES) {
+      float r8[8];
+      unpack8(rv[k], r8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[k][i] = round_bf16(r8[i] + v[k][i]);
+      const int c = threadIdx.x + k * blockDim.x;
+      if (WRITE_H && c < chunks) st_global(h + base + c * 8, pack8(v[k]));
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[k][i], v[k][i], ss);
+  }
+  const float tot = block_sum(ss, slots, 0);
+  const float r = rsqrtf(tot / static_cast<float>(N) + eps);
+  if (WRITE_RSTD && threadIdx.x == 0) rstd[row] = r;
+
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < chunks) {
+      float wf[8], o[8];
+      unpack8(wv[k], wf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = (v[k][i] * r) * wf[i];
+      st_global(y + base + c * 8, pack8(o));
+    }
+  }
+}
+
+template <bool HAS_RES, bool WRITE_H, bool WRITE_RSTD>
+__global__ void __launch_bounds__(256)
+rmsnorm_fwd_generic(const uint16_t* __restrict__ x, const uint16_t* __restrict__ res,
+                    const uint16_t* __restrict__ w, uint16_t* __restrict__ h,
+                    uint16_t* __restrict__ y, float* __restrict__ rstd, int64_t N, float eps) {
+  __shared__ float slots[2][32];
+  const int64_t row = blockIdx.x;
+  const size_t base = static_cast<size_t>(row) * N;
+  float ss = 0.f;
+  for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+    float v = bf16_to_f(x[base + n]);
+    if (HAS_RES) {
+      v = round_bf16(bf16_to_f(res[base + n]) + v);
+      if (WRITE_H) h[base + n] = f_to_bf16(v);
+    }
+    ss = fmaf(v, v, ss);
+  }
+  const float tot = block_sum(ss, slots, 0);
+  const float r = rsqrtf(tot / static_cast<float>(N) + eps);
+  if (WRITE_RSTD && threadIdx.x == 0) rstd[row] = r;
+  for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+    float v = bf16_to_f(x[base + n]);
+    if (HAS_RES) v = round_bf16(bf16_to_f(res[base + n]) + v);
+    y[base + n] = f_to_bf16((v * r) * bf16_to_f(w[n]));
+  }
+}
+
+template <bool HAS_RES, bool WRITE_H, bool WRITE_RSTD>
+int launch_fwd_t(const RowCfg& cfg, const uint16_t* x, const uint16_t* res,
+                 const uint16_t* w, uint16_t* h, uint16_t* y, float* rstd,
+                 int64_t M, int64_t N, float eps, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(M));
+  switch (cfg.vpt) {
+    case 2:
+      rmsnorm_fwd_vec<2, HAS_RES, WRITE_H, WRITE_RSTD>
+          <<<grid, cfg.threads, 0, s>>>(x, res, w, h, y, rstd, static_cast<int>(N), eps);
+      break;
+    case 4:
+      rmsnorm_fwd_vec<4, HAS_RES, WRITE_H, WRITE_RSTD>
+          <<<grid, cfg.threads, 0, s>>>(x, res, w, h, y, rstd, static_cast<int>(N), eps);
+      break;
+    default:
+      rmsnorm_fwd_generic<HAS_RES, WRITE_H, WRITE_RSTD>
+          <<<grid, 256, 0, s>>>(x, res, w, h, y, rstd, N, eps);
+  }
+  return check_launch();
+}
+
+int launch_fwd(const void* res, const void* x, const void* w, void* h, void* y,
+               float* rstd, int64_t M, int64_t N, float eps, cudaStream_t s) {
+  if (!x || !w || !y) return FRAG_ERR_INVALID_ARG;
+  if (M < 0 || N < 0) return FRAG_ERR_INVALID_ARG;
+  if (M == 0) return FRAG_OK;
+  if (N == 0 || M > 0x7fffffffLL) return FRAG_ERR_SHAPE;
+  bool aligned = aligned16(x) && aligned16(w) && aligned16(y);
+  if (res) aligned = aligned && aligned16(res);
+  if (h) aligned = aligned && aligned16(h);
+  const RowCfg cfg = pick_row_cfg(N, aligned);
+  auto X = static_cast<const uint16_t*>(x);
+  auto R = static_cast<const uint16_t*>(res);
+  auto W = static_cast<const uint16_t*>(w);
+  auto H = static_cast<uint16_t*>(h);
+  auto Y = static_cast<uint16_t*>(y);
+  if (!res) {
+    return rstd ? launch_fwd_t<false, false, true>(cfg, X, R, W, H, Y, rstd, M, N, eps, s)
+                : launch_fwd_t<false, false, false>(cfg, X, R, W, H, Y, rstd, M, N, eps, s);
+  }
+  if (h) {
+    return rstd ? launch_fwd_t<true, true, true>(cfg, X, R, W, H, Y, rstd, M, N, eps, s)
+                : launch_fwd_t<true, true, false>(cfg, X, R, W, H, Y, rstd, M, N, eps, s);
+  }
+  return rstd ? launch_fwd_t<true, false, true>(cfg, X, R, W, H, Y, rstd, M, N, eps, s)
+              : launch_fwd_t<true, false, false>(cfg, X, R, W, H, Y, rstd, M, N, eps, s);
+}
+
+// ----------------------------------------------------------------- backward
+
+struct BwdIn {
+  const uint16_t* dy;
+  const uint16_t* dy2;
+  const uint16_t* x;
+  const float* rstd;
+  const uint16_t* w;
+  const uint16_t* dres;
+  uint16_t* dx;
+  float* partials;  // [G, N]
+  float* rws;       // [M] rstd scratch (generic path)
+};
+
+// One row block per CTA: rows [b*R, min(M, (b+1)*R)).  The next row's inputs
+// are loaded before the current row is reduced, so each thread keeps up to two
+// rows of loads in flight; rows stay packed (bf16) in registers and are
+// widened on the fly.  dweight partial sums stay in registers (each thread
+// owns fixed columns) and are written once per block.
+template <int VPT, bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
+__device__ __forceinline__ void bwd_load_row(const BwdIn& p, int64_t row, int N, int chunks,
+                                             uint4 (&dy)[VPT], uint4 (&xx)[VPT],
+                                             uint4 (&dy2)[VPT], uint4 (&dr)[VPT], float& rr) {
+  const size_t base = static_cast<size_t>(row) * N;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < chunks) {
+      dy[k] = ld_stream(p.dy + base + c * 8);
+      xx[k] = ld_stream(p.x + base + c * 8);
+      if (HAS_DY2) dy2[k] = ld_stream(p.dy2 + base + c * 8);
+      if (HAS_DRES) dr[k] = ld_stream(p.dres + base + c * 8);
+    } else {
+      dy[k] = xx[k] = make_uint4(0, 0, 0, 0);
+      if (HAS_DY2) dy2[k] = make_uint4(0, 0, 0, 0);
+      if (HAS_DRES) dr[k] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  if (!RECOMPUTE) rr = __ldg(p.rstd + row);
+}
+
+template <int VPT, bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
+__global__ void __launch_bounds__(512)
+rmsnorm_bwd_vec(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block) {
+  __shared__ float2 slots[2][32];
+  const int chunks = N >> 3;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+  const int64_t r1 = min(M, r0 + rows_per_block);
+  const float invN = 1.0f / static_cast<float>(N);
+
+  float acc[VPT][8];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
+
+  uint4 cdy[VPT], cx[VPT], cdy2[VPT], cdr[VPT];
+  float cr = 0.f;
+  if (r0 < r1) bwd_load_row<VPT, HAS_DY2, HAS_DRES, RECOMPUTE>(p, r0, N, chunks, cdy, cx, cdy2, cdr, cr);
+  int parity = 0;
+  for (int64_t row = r0; row < r1; ++row) {
+    uint4 ndy[VPT], nx[VPT], ndy2[VPT], ndr[VPT];
+    float nr = 0.f;
+    if (row + 1 < r1) bwd_load_row<VPT, HAS_DY2, HAS_DRES, RECOMPUTE>(p, row + 1, N, chunks, ndy, nx, ndy2, ndr, nr);
+
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      const uint4 wv = (c < chunks) ? ld_cached(p.w + c * 8) : make_uint4(0, 0, 0, 0);
+      float g[8], xf[8], wf[8];
+      unpack8(cdy[k], g);
+      if (HAS_DY2) {
+        // The summed gradient is a bf16 tensor in the reference graph.
+        float g2[8];
+        unpack8(cdy2[k], g2);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) g[i] = g[i] + g2[i];
+        cdy[k] = pack8(g);
+        unpack8(cdy[k], g);
+      }
+      unpack8(cx[k], xf);
+      unpack8(wv, wf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (RECOMPUTE) s1 = fmaf(xf[i], xf[i], s1);
+        s2 = fmaf(xf[i], g[i] * wf[i], s2);
+      }
+    }
+    const float2 tot = block_sum2(make_float2(s1, s2), slots, parity);
+    parity ^= 1;
+    const float r = RECOMPUTE ? rsqrtf(tot.x * invN + eps) : cr;
+    // mean(xhat * gw) = r * sum(x * gw) / N
+    const float cmean = r * tot.y * invN;
+    const size_t base = static_cast<size_t>(row) * N;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      const uint4 wv = (c < chunks) ? ld_cached(p.w + c * 8) : make_uint4(0, 0, 0, 0);
+      float g[8], xf[8], wf[8], o[8];
+      unpack8(cdy[k], g);
+      unpack8(cx[k], xf);
+      unpack8(wv, wf);
+      if (HAS_DRES) unpack8(cdr[k], o);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float xhat = xf[i] * r;
+        const float dx = (g[i] * wf[i] - xhat * cmean) * r;
+        acc[k][i] = fmaf(g[i], xhat, acc[k][i]);
+        o[i] = HAS_DRES ? o[i] + round_bf16(dx) : dx;
+      }
+      if (c < chunks) st_global(p.dx + base + c * 8, pack8(o));
+    }
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      cdy[k] = ndy[k];
+      cx[k] = nx[k];
+      if (HAS_DY2) cdy2[k] = ndy2[k];
+      if (HAS_DRES) cdr[k] = ndr[k];
+    }
+    cr = nr;
+  }
+
+  float* part = p.partials + static_cast<size_t>(blockIdx.x) * N;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < chunks) {
+      float4* dst = reinterpret_cast<float4*>(part + c * 8);
+      dst[0] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+      dst[1] = make_float4(acc[k][4], acc[k][5], acc[k][6], acc[k][7]);
+    }
+  }
+}
+
+// Generic backward, pass 1: dx per row (one CTA per row), rstd copied or
+// recomputed into p.rws for pass 2.
+template <bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
+__global__ void __launch_bounds__(256)
+rmsnorm_bwd_generic_dx(BwdIn p, int64_t N, float eps) {
+  __shared__ float2 slots[2][32];
+  const int64_t row = blockIdx.x;
+  const size_t base = static_cast<size_t>(row) * N;
+  float s1 = 0.f, s2 = 0.f;
+  for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+    float g = bf16_to_f(p.dy[base + n]);
+    if (HAS_DY2) g = round_bf16(g + bf16_to_f(p.dy2[base + n]));
+    const float xf = bf16_to_f(p.x[base + n]);
+    if (RECOMPUTE) s1 = fmaf(xf, xf, s1);
+    s2 = fmaf(xf, g * bf16_to_f(p.w[n]), s2);
+  }
+  const float2 tot = block_sum2(make_float2(s1, s2), slots, 0);
+  const float invN = 1.0f / static_cast<float>(N);
+  const float r = RECOMPUTE ? rsqrtf(tot.x * invN + eps) : p.rstd[row];
+  if (threadIdx.x == 0) p.rws[row] = r;
+  const float cmean = r * tot.y * invN;
+  for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+    float g = bf16_to_f(p.dy[base + n]);
+    if (HAS_DY2) g = round_bf16(g + bf16_to_f(p.dy2[base + n]));
+    const float xhat = bf16_to_f(p.x[base + n]) * r;
+    const float dx = (g * bf16_to_f(p.w[n]) - xhat * cmean) * r;
+    const float o = HAS_DRES ? bf16_to_f(p.dres[base + n]) + round_bf16(dx) : dx;
+    p.dx[base + n] = f_to_bf16(o);
+  }
+}
+
+// Generic backward, pass 2: dweight partials, one thread per column per block.
+template <bool HAS_DY2>
+__global__ void __launch_bounds__(256)
+rmsnorm_bwd_generic_dw(BwdIn p, int64_t M, int64_t N, int64_t rows_per_block) {
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (col >= N) return;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * rows_per_block;
+  const int64_t r1 = min(M, r0 + rows_per_block);
+  float acc = 0.f;
+  for (int64_t row = r0; row < r1; ++row) {
+    const size_t i = static_cast<size_t>(row) * N + col;
+    float g = bf16_to_f(p.dy[i]);
+    if (HAS_DY2) g = round_bf16(g + bf16_to_f(p.dy2[i]));
+    acc = fmaf(g, bf16_to_f(p.x[i]) * p.rws[row], acc);
+  }
+  p.partials[static_cast<size_t>(blockIdx.y) * N + col] = acc;
+}
+
+// dw[n] = sum_{b=0}^{G-1} partials[b, n]: warp w adds blocks w, w+8, ... in
+// order, then the 8 warp sums are added in warp order.  Fixed order, so the
+// result is bitwise reproducible.
+template <bool VEC>
+__global__ void __launch_bounds__(256)
+dw_reduce_kernel(const float* __restrict__ partials, int64_t G, int64_t N,
+                 float* __restrict__ dw, uint16_t* __restrict__ dw_bf16) {
+  __shared__ float red[8][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * 128 + lane * 4;
+  float a[4] = {0.f, 0.f, 0.f, 0.f};
+  if (VEC) {
+    if (c0 < N) {
+      for (int64_t b = warp; b < G; b += 8) {
+        const float4 v = *reinterpret_cast<const float4*>(partials + b * N + c0);
+        a[0] += v.x; a[1] += v.y; a[2] += v.z; a[3] += v.w;
+      }
+    }
+  } else {
+    for (int64_t b = warp; b < G; b += 8) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (c0 + j < N) a[j] += partials[b * N + c0 + j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) red[warp][lane * 4 + j] = a[j];
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int64_t col = static_cast<int64_t>(blockIdx.x) * 128 + threadIdx.x;
+    if (col < N) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) s += red[w][threadIdx.x];
+      if (dw) dw[col] = s;
+      if (dw_bf16) dw_bf16[col] = f_to_bf16(s);
+    }
+  }
+}
+
+int launch_dw_reduce(const float* partials, int64_t G, int64_t N, float* dw,
+                     uint16_t* dw_bf16, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(ceil_div(N, 128)));
+  if (N % 4 == 0 && aligned16(partials))
+    dw_reduce_kernel<true><<<grid, 256, 0, s>>>(partials, G, N, dw, dw_bf16);
+  else
+    dw_reduce_kernel<false><<<grid, 256, 0, s>>>(partials, G, N, dw, dw_bf16);
+  return check_launch();
+}
+
+// Row-block plan shared by the workspace query and the launch: the number of
+// blocks G is the number of CTAs of the heaviest vector variant that fit on
+// the device at once, so the whole grid runs as one wave.
+struct BwdPlan {
+  RowCfg cfg;
+  int64_t G;
+  int64_t rows_per_block;
+};
+
+int vec_blocks_per_sm(int vpt, int threads) {
+  int n = 0;
+  cudaError_t e = cudaSuccess;
+  switch (vpt) {
+    case 2: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, rmsnorm_bwd_vec<2, true, true, true>, threads, 0); break;
+    default: n = 8;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    n = 1;
+  }
+  return std::max(1, n);
+}
+
+BwdPlan make_bwd_plan(int64_t M, int64_t N, bool aligned) {
+  BwdPlan pl;
+  pl.cfg = pick_row_cfg(N, aligned);
+  // The backward keeps two rows of up to four inputs in registers: only the
+  // 2-chunks-per-thread variant fits (N <= 8192 at 512 threads).
+  if (pl.cfg.vpt != 2) pl.cfg = RowCfg{0, 256};
+  int sms = sm_count();
+  if (sms <= 0) sms = 148;
+  int64_t target = static_cast<int64_t>(sms) * vec_blocks_per_sm(pl.cfg.vpt, pl.cfg.threads);
+  if (pl.cfg.vpt == 0) target = static_cast<int64_t>(sms) * 4;
+  target = std::max<int64_t>(1, std::min<int64_t>(target, M));
+  pl.rows_per_block = ceil_div(M, target);
+  pl.G = ceil_div(M, pl.rows_per_block);
+  return pl;
+}
+
+size_t bwd_workspace_bytes(const BwdPlan& pl, int64_t M, int64_t N) {
+  return align_up(static_cast<size_t>(pl.G) * N * sizeof(float), 256) +
+         align_up(static_cast<size_t>(M) * sizeof(float), 256);
+}
+
+template <bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
+int launch_bwd_t(const BwdPlan& pl, BwdIn p, int64_t M, int64_t N, float eps, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(pl.G));
+  const int T = pl.cfg.threads;
+  switch (pl.cfg.vpt) {
+    case 2:
+      rmsnorm_bwd_vec<2, HAS_DY2, HAS_DRES, RECOMPUTE><<<grid, T, 0, s>>>(p, M, static_cast<int>(N), eps, pl.rows_per_block);
+      break;
+    default: {
+      rmsnorm_bwd_generic_dx<HAS_DY2, HAS_DRES, RECOMPUTE>
+          <<<dim3(static_cast<unsigned>(M)), 256, 0, s>>>(p, N, eps);
+      int st = check_launch();
+      if (st != FRAG_OK) return st;
+      const dim3 g2(static_cast<unsigned>(ceil_div(N, 256)), static_cast<unsigned>(pl.G));
+      rmsnorm_bwd_generic_dw<HAS_DY2><<<g2, 256, 0, s>>>(p, M, N, pl.rows_per_block);
+    }
+  }
+  return check_launch();
+}
+
+}  // namespace
+}  // namespace frag
+
+using namespace frag;
+
+extern "C" {
+
+int frag_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int64_t M,
+                     int64_t N, float eps, frag_stream_t stream) {
+  return launch_fwd(nullptr, x, w, nullptr, y, rstd, M, N, eps,
+                    reinterpret_cast<cudaStream_t>(stream));
+}
+
+int frag_add_rmsnorm_fwd(const void* res, const void* x, const void* w, void* h, void* y,
+                         float* rstd, int64_t M, int64_t N, float eps,
+                         frag_stream_t stream) {
+  if (!res) return FRAG_ERR_INVALID_ARG;
+  return launch_fwd(res, x, w, h, y, rstd, M, N, eps, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t frag_rmsnorm_bwd_workspace_bytes(int64_t M, int64_t N) {
+  if (M <= 0 || N <= 0) return 0;
+  // The generic plan (unaligned callers) never needs more than the vector one
+  // for the same M: both use at most sm_count * blocks_per_sm blocks.
+  const BwdPlan a = make_bwd_plan(M, N, true);
+  const BwdPlan b = make_bwd_plan(M, N, false);
+  return std::max(bwd_workspace_bytes(a, M, N), bwd_workspace_bytes(b, M, N));
+}
+
+int64_t frag_rmsnorm_bwd_num_blocks(int64_t M, int64_t N) {
+  if (M <= 0 || N <= 0) return 0;
+  return make_bwd_plan(M, N, true).G;
+}
+
+int frag_dw_reduce(const float* partials, int64_t G, int64_t N, float* dw, void* dw_bf16,
+                   frag_stream_t stream) {
+  if (!partials || (!dw && !dw_bf16) || G < 0 || N < 0) return FRAG_ERR_INVALID_ARG;
+  if (N == 0) return FRAG_OK;
+  return launch_dw_reduce(partials, G, N, dw, static_cast<uint16_t*>(dw_bf16),
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int frag_rmsnorm_bwd(const void* dy, const void* dy2, const void* x, const float* rstd,
+                     const void* w, const void* dres, void* dx_out, float* dw, void* dw_bf16,
+                     int64_t M, int64_t N, float eps, void* workspace,
+                     size_t workspace_bytes, frag_stream_t stream) {
+  if (!dy || !x || !w || !dx_out) return FRAG_ERR_INVALID_ARG;
+  if (M < 0 || N < 0) return FRAG_ERR_INVALID_ARG;
+  if (N == 0 && M > 0) return FRAG_ERR_SHAPE;
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL) return FRAG_ERR_SHAPE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (M == 0) {
+    // Empty batch: dweight is an empty sum.
+    if (dw && cuda_status(cudaMemsetAsync(dw, 0, N * sizeof(float), s)) != FRAG_OK)
+      return FRAG_ERR_CUDA;
+    if (dw_bf16 && cuda_status(cudaMemsetAsync(dw_bf16, 0, N * 2, s)) != FRAG_OK)
+      return FRAG_ERR_CUDA;
+    return FRAG_OK;
+  }
+  bool aligned = aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx_out);
+  if (dy2) aligned = aligned && aligned16(dy2);
+  if (dres) aligned = aligned && aligned16(dres);
+  const BwdPlan pl = make_bwd_plan(M, N, aligned);
+  if (!workspace || workspace_bytes < bwd_workspace_bytes(pl, M, N)) return FRAG_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return FRAG_ERR_ALIGN;
+
+  BwdIn p;
+  p.dy = static_cast<const uint16_t*>(dy);
+  p.dy2 = static_cast<const uint16_t*>(dy2);
+  p.x = static_cast<const uint16_t*>(x);
+  p.rstd = rstd;
+  p.w = static_cast<const uint16_t*>(w);
+  p.dres = static_cast<const uint16_t*>(dres);
+  p.dx = static_cast<uint16_t*>(dx_out);
+  p.partials = static_cast<float*>(workspace);
+  p.rws = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                   align_up(static_cast<size_t>(pl.G) * N * sizeof(float), 256));
+
+  const bool rc = (rstd == nullptr);
+  int st;
+  if (dy2) {
+    if (dres) st = rc ? launch_bwd_t<true, true, true>(pl, p, M, N, eps, s) : launch_bwd_t<true, true, false>(pl, p, M, N, eps, s);
+    else st = rc ? launch_bwd_t<true, false, true>(pl, p, M, N, eps, s) : launch_bwd_t<true, false, false>(pl, p, M, N, eps, s);
+  } else {
+    if (dres) st = rc ? launch_bwd_t<false, true, true>(pl, p, M, N, eps, s) : launch_bwd_t<false, true, false>(pl, p, M, N, eps, s);
+    else st = rc ? launch_bwd_t<false, false, true>(pl, p, M, N, eps, s) : launch_bwd_t<false, false, false>(pl, p, M, N, eps, s);
+  }
+  if (st != FRAG_OK) return st;
+  if (dw || dw_bf16)
+    return launch_dw_reduce(p.partials, pl.G, N, dw, static_cast<uint16_t*>(dw_bf16), s);
+  return FRAG_OK;
+}
+
+}  // extern "C"

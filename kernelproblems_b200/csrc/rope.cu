@@ -1,0 +1,276 @@
+// rope.cu — rotary position embedding (forward and its inverse) on q and k.
+//
+// Reference math (v8/c8c60d8f7015/problem.py:18-70): x is widened to fp32,
+// viewed as complex pairs, multiplied by freqs_cis[pos] and rounded back to
+// bf16.  Here the pair layout is a template parameter:
+//   INTERLEAVED  pairs (x[2j], x[2j+1])        (the reference's view_as_complex)
+//   NEOX         pairs (x[j], x[j + D/2])      (rotate-half)
+// and (cos, sin) either come from the caller's complex64 table (the
+// reference's freqs_cis input) or are evaluated in registers from
+//   angle_j = float(pos) * inv_freq[j],  inv_freq[j] = theta^(-2j/D)
+// with the accurate sincosf, so no cache tensor is read from HBM.
+// The backward is the same rotation by the conjugate (v6/03d64c25b654/problem.py:12-43
+// multiplies the incoming gradient by conj(freqs_cis)).
+//
+// Vector path: one warp per token; D/16 lanes per head, each lane owns the 8
+// pairs with frequency indices 8j..8j+7, so its 8 (cos, sin) values are
+// computed once per token and reused for every head of q and k.
+#include <math.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace frag {
+namespace {
+
+constexpr int kMaxHalf = 256;  // D <= 512
+
+struct RopeT {
+  const uint16_t* x;
+  uint16_t* out;
+  int H;
+  int64_t xsb, xss, xsh, osb, oss, osh;
+};
+
+struct RopeP {
+  RopeT t[2];
+  int nt;
+  int64_t B, S;
+  int D;
+  const void* pos;
+  int pos_dtype;
+  int64_t psb, pss;
+  const float* freqs;  // complex64 as (re, im) float pairs
+  int64_t fstride;     // complex elements per table row
+  float sign;          // +1 forward, -1 inverse
+  float inv_freq[kMaxHalf];
+};
+
+__device__ __forceinline__ int64_t load_pos(const RopeP& p, int64_t b, int64_t s) {
+  if (p.pos_dtype == FRAG_POS_I32)
+    return __ldg(static_cast<const int32_t*>(p.pos) + b * p.psb + s * p.pss);
+  if (p.pos_dtype == FRAG_POS_I64)
+    return __ldg(static_cast<const int64_t*>(p.pos) + b * p.psb + s * p.pss);
+  return s;
+}
+
+template <bool NEOX>
+__device__ __forceinline__ void rotate(const uint4& a, const uint4& c, const float (&cs)[8],
+                                       const float (&sn)[8], uint4& oa, uint4& oc) {
+  float fa[8], fc[8], ra[8], rc[8];
+  unpack8(a, fa);
+  unpack8(c, fc);
+  if (NEOX) {
+    // a = x[8j..8j+8), c = x[D/2+8j..): pair i is (fa[i], fc[i]).
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ra[i] = fa[i] * cs[i] - fc[i] * sn[i];
+      rc[i] = fc[i] * cs[i] + fa[i] * sn[i];
+    }
+  } else {
+    // a, c = x[16j..16j+16): pairs (re, im) at even/odd positions.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float re = fa[2 * i], im = fa[2 * i + 1];
+      ra[2 * i] = re * cs[i] - im * sn[i];
+      ra[2 * i + 1] = re * sn[i] + im * cs[i];
+      const float re2 = fc[2 * i], im2 = fc[2 * i + 1];
+      rc[2 * i] = re2 * cs[4 + i] - im2 * sn[4 + i];
+      rc[2 * i + 1] = re2 * sn[4 + i] + im2 * cs[4 + i];
+    }
+  }
+  oa = pack8(ra);
+  oc = pack8(rc);
+}
+
+template <int LPH, bool NEOX, bool TABLE>
+__global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
+  __shared__ float sfreq[kMaxHalf];
+  const int half = p.D >> 1;
+  if (!TABLE)
+    for (int i = threadIdx.x; i < half; i += blockDim.x) sfreq[i] = p.inv_freq[i];
+  __syncthreads();
+  constexpr int HPI = 32 / LPH;  // heads per warp iteration
+  constexpr int UNR = 4;
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (tok >= p.B * p.S) return;
+  const int64_t b = tok / p.S, s = tok - b * p.S;
+  const int64_t pos = load_pos(p, b, s);
+  const int j = lane % LPH, hs = lane / LPH;
+
+  float cs[8], sn[8];
+  if (TABLE) {
+    const float4* f = reinterpret_cast<const float4*>(p.freqs + 2 * (pos * p.fstride + 8 * j));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = __ldg(f + i);
+      cs[2 * i] = v.x;
+      sn[2 * i] = v.y * p.sign;
+      cs[2 * i + 1] = v.z;
+      sn[2 * i + 1] = v.w * p.sign;
+    }
+  } else {
+    const float fp = static_cast<float>(pos);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float sv, cv;
+      sincosf(fp * sfreq[8 * j + i], &sv, &cv);
+      cs[i] = cv;
+      sn[i] = sv * p.sign;
+    }
+  }
+
+  // Element offsets of this lane's two 16-byte chunks within a head.
+  const int oa = NEOX ? 8 * j : 16 * j;
+  const int oc = NEOX ? half + 8 * j : 16 * j + 8;
+#pragma unroll
+  for (int ti = 0; ti < 2; ++ti) {
+    if (ti >= p.nt) break;
+    const RopeT& T = p.t[ti];
+    const uint16_t* xb = T.x + b * T.xsb + s * T.xss;
+    uint16_t* ob = T.out + b * T.osb + s * T.oss;
+    for (int h0 = hs; h0 < T.H; h0 += HPI * UNR) {
+      uint4 va[UNR], vc[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int h = h0 + u * HPI;
+        if (h < T.H) {
+          va[u] = ld_stream(xb + h * T.xsh + oa);
+          vc[u] = ld_stream(xb + h * T.xsh + oc);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int h = h0 + u * HPI;
+        if (h < T.H) {
+          uint4 ra, rc;
+          rotate<NEOX>(va[u], vc[u], cs, sn, ra, rc);
+          st_global(ob + h * T.osh + oa, ra);
+          st_global(ob + h * T.osh + oc, rc);
+        }
+      }
+    }
+  }
+}
+
+// Any even D, any strides: one CTA per token, one thread per (head, pair).
+template <bool NEOX, bool TABLE>
+__global__ void __launch_bounds__(256) rope_generic(const RopeP p) {
+  __shared__ float sfreq[kMaxHalf];
+  const int half = p.D >> 1;
+  if (!TABLE)
+    for (int i = threadIdx.x; i < half; i += blockDim.x) sfreq[i] = p.inv_freq[i];
+  __syncthreads();
+  const int64_t tok = blockIdx.x;
+  const int64_t b = tok / p.S, s = tok - b * p.S;
+  const int64_t pos = load_pos(p, b, s);
+#pragma unroll
+  for (int ti = 0; ti < 2; ++ti) {
+    if (ti >= p.nt) break;
+    const RopeT& T = p.t[ti];
+    const uint16_t* xb = T.x + b * T.xsb + s * T.xss;
+    uint16_t* ob = T.out + b * T.osb + s * T.oss;
+    for (int64_t q = threadIdx.x; q < static_cast<int64_t>(T.H) * half; q += blockDim.x) {
+      const int h = static_cast<int>(q / half), jj = static_cast<int>(q - static_cast<int64_t>(h) * half);
+      float cv, sv;
+      if (TABLE) {
+        cv = p.freqs[2 * (pos * p.fstride + jj)];
+        sv = p.freqs[2 * (pos * p.fstride + jj) + 1];
+      } else {
+        sincosf(static_cast<float>(pos) * sfreq[jj], &sv, &cv);
+      }
+      sv *= p.sign;
+      const int ia = NEOX ? jj : 2 * jj;
+      const int ic = NEOX ? jj + half : 2 * jj + 1;
+      const float a = bf16_to_f(xb[h * T.xsh + ia]);
+      const float c = bf16_to_f(xb[h * T.xsh + ic]);
+      const float ra = a * cv - c * sv;
+      const float rc = NEOX ? c * cv + a * sv : a * sv + c * cv;
+      ob[h * T.osh + ia] = f_to_bf16(ra);
+      ob[h * T.osh + ic] = f_to_bf16(rc);
+    }
+  }
+}
+
+template <bool NEOX, bool TABLE>
+int launch_rope_t(const RopeP& p, bool vec, cudaStream_t s) {
+  const int64_t tokens = p.B * p.S;
+  if (vec) {
+    const dim3 grid(static_cast<unsigned>(ceil_div(tokens, 8)));
+    switch (p.D / 16) {
+      case 1: rope_vec<1, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
+      case 2: rope_vec<2, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
+      case 4: rope_vec<4, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
+      case 8: rope_vec<8, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
+      case 16: rope_vec<16, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
+      case 32: rope_vec<32, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
+      default: return FRAG_ERR_SHAPE;
+    }
+  } else {
+    rope_generic<NEOX, TABLE><<<dim3(static_cast<unsigned>(tokens)), 256, 0, s>>>(p);
+  }
+  return check_launch();
+}
+
+}  // namespace
+}  // namespace frag
+
+using namespace frag;
+
+extern "C" int frag_rope(const frag_rope_tensor* tensors, int num_tensors, int64_t B, int64_t S,
+                         int64_t D, const void* pos, int pos_dtype, int64_t pos_stride_b,
+                         int64_t pos_stride_s, const float* freqs, int64_t freqs_stride,
+                         float theta, int layout, int inverse, frag_stream_t stream) {
+  if (!tensors || num_tensors < 1 || num_tensors > 2) return FRAG_ERR_INVALID_ARG;
+  if (B < 0 || S < 0 || D < 0) return FRAG_ERR_INVALID_ARG;
+  if (layout != FRAG_ROPE_NEOX && layout != FRAG_ROPE_INTERLEAVED) return FRAG_ERR_INVALID_ARG;
+  if (pos_dtype != FRAG_POS_NONE && pos_dtype != FRAG_POS_I32 && pos_dtype != FRAG_POS_I64)
+    return FRAG_ERR_INVALID_ARG;
+  if (pos_dtype != FRAG_POS_NONE && !pos) return FRAG_ERR_INVALID_ARG;
+  if (B * S == 0) return FRAG_OK;
+  if (D == 0 || D % 2 != 0 || D / 2 > kMaxHalf) return FRAG_ERR_SHAPE;
+  if (B * S > 0x7fffffffLL) return FRAG_ERR_SHAPE;
+
+  RopeP p;
+  p.nt = num_tensors;
+  p.B = B;
+  p.S = S;
+  p.D = static_cast<int>(D);
+  p.pos = pos;
+  p.pos_dtype = pos_dtype;
+  p.psb = pos_stride_b;
+  p.pss = pos_stride_s;
+  p.freqs = freqs;
+  p.fstride = freqs_stride;
+  p.sign = inverse ? -1.0f : 1.0f;
+  const int half = static_cast<int>(D / 2);
+  for (int i = 0; i < kMaxHalf; ++i) p.inv_freq[i] = 0.f;
+  if (!freqs) {
+    if (!(theta > 0.f)) return FRAG_ERR_INVALID_ARG;
+    for (int i = 0; i < half; ++i)
+      p.inv_freq[i] = static_cast<float>(1.0 / pow(static_cast<double>(theta),
+                                                   static_cast<double>(2 * i) / static_cast<double>(D)));
+  }
+
+  bool vec = D % 16 == 0 && (D / 16) <= 32 && (32 % (D / 16)) == 0;
+  if (freqs) vec = vec && aligned16(freqs) && freqs_stride % 2 == 0;
+  p.t[1] = RopeT{nullptr, nullptr, 0, 0, 0, 0, 0, 0, 0};
+  for (int i = 0; i < num_tensors; ++i) {
+    const frag_rope_tensor& t = tensors[i];
+    if (t.H < 0 || t.H > 0x7fffffffLL) return FRAG_ERR_SHAPE;
+    if (t.H > 0 && (!t.x || !t.out)) return FRAG_ERR_INVALID_ARG;
+    p.t[i] = RopeT{static_cast<const uint16_t*>(t.x), static_cast<uint16_t*>(t.out),
+                   static_cast<int>(t.H), t.x_stride_b, t.x_stride_s, t.x_stride_h,
+                   t.out_stride_b, t.out_stride_s, t.out_stride_h};
+    const int64_t st[6] = {t.x_stride_b, t.x_stride_s, t.x_stride_h,
+                           t.out_stride_b, t.out_stride_s, t.out_stride_h};
+    for (int k = 0; k < 6; ++k) vec = vec && (st[k] % 8 == 0);
+    vec = vec && aligned16(t.x) && aligned16(t.out);
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool neox = layout == FRAG_ROPE_NEOX;
+  if (neox) return freqs ? launch_rope_t<true, true>(p, vec, s) : launch_rope_t<true, false>(p, vec, s);
+  return freqs ? launch_rope_t<false, true>(p, vec, s) : launch_rope_t<false, false>(p, vec, s);
+}

@@ -1,0 +1,62 @@
+// status.cu — version, status strings, per-thread CUDA error record and the
+// cached device queries used to size launches.
+#include <mutex>
+
+#include "common.cuh"
+
+namespace frag {
+
+static thread_local int g_last_cuda_error = 0;
+
+void set_last_cuda_error(cudaError_t e) { g_last_cuda_error = static_cast<int>(e); }
+
+int current_device() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return d;
+}
+
+int sm_count() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int d = current_device();
+  if (d < 0 || d >= 64) return 0;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[d] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    cache[d] = n;
+  }
+  return cache[d];
+}
+
+}  // namespace frag
+
+extern "C" {
+
+const char* frag_version(void) { return "libfrag 0.1.0 (sm_100a)"; }
+
+const char* frag_status_string(int status) {
+  switch (status) {
+    case FRAG_OK: return "ok";
+    case FRAG_ERR_INVALID_ARG: return "invalid argument (null pointer or negative size)";
+    case FRAG_ERR_SHAPE: return "unsupported shape";
+    case FRAG_ERR_ALIGN: return "misaligned pointer or stride";
+    case FRAG_ERR_WORKSPACE: return "workspace missing or too small";
+    case FRAG_ERR_CUDA: return "CUDA runtime error";
+    case FRAG_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+int frag_last_cuda_error(void) { return frag::g_last_cuda_error; }
+
+int frag_device_sm_count(void) { return frag::sm_count(); }
+
+}  // extern "C"

@@ -1,0 +1,375 @@
+"""Functional API over libfrag.so for torch CUDA tensors.
+
+Every op validates dtypes/shapes on the host, allocates its outputs (and any
+workspace) with torch on the input's device, and launches the CUDA kernels
+through the C ABI on the current stream.  Nothing here computes on the CPU:
+if the library is missing the call raises.
+
+Embedding ids are range-checked on the device.  A bad id writes a zero row and
+sets a flag in a per-device status word; ``check_status()`` synchronises and
+raises ``IndexError`` if any flag is set.  Set ``FRAG_SYNC_CHECK=1`` to check
+after every embedding call (what torch's device-side assert would catch).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from contextlib import contextmanager
+
+import torch
+
+from . import _lib
+from ._lib import FragError
+
+__all__ = [
+    "FragError",
+    "rmsnorm_fwd",
+    "add_rmsnorm_fwd",
+    "rmsnorm_bwd",
+    "rmsnorm_bwd_workspace_bytes",
+    "rmsnorm_bwd_num_blocks",
+    "dw_reduce",
+    "embedding_fwd",
+    "embedding_bwd",
+    "rope",
+    "check_status",
+    "reset_status",
+]
+
+_SYNC_CHECK = os.environ.get("FRAG_SYNC_CHECK", "0") not in ("", "0")
+_status_words: dict[int, torch.Tensor] = {}
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(dev: torch.device):
+    return C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+@contextmanager
+def _on_device(dev: torch.device):
+    if dev.type != "cuda":
+        raise ValueError(f"kernelproblems_b200 ops need CUDA tensors, got device {dev}")
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if torch.cuda.current_device() == idx:
+        yield
+    else:
+        with torch.cuda.device(idx):
+            yield
+
+
+def _need(t: torch.Tensor, name: str, dtype: torch.dtype, dev: torch.device | None = None):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if dev is not None and t.device != dev:
+        raise ValueError(f"{name} is on {t.device}, expected {dev}")
+
+
+def _status_word(dev: torch.device) -> torch.Tensor:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    w = _status_words.get(idx)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_words[idx] = w
+    return w
+
+
+def check_status(device: torch.device | int | None = None) -> None:
+    """Synchronise and raise IndexError if a kernel flagged an out-of-range id."""
+    devs = list(_status_words) if device is None else [torch.device("cuda", device).index
+                                                        if isinstance(device, int) else device.index]
+    for idx in devs:
+        w = _status_words.get(idx)
+        if w is None:
+            continue
+        v = int(w.item())
+        if v & _lib.FRAG_DEVFLAG_INDEX_OOB:
+            w.zero_()
+            raise IndexError("embedding: an index was outside [0, num_embeddings)")
+
+
+def reset_status() -> None:
+    for w in _status_words.values():
+        w.zero_()
+
+
+# ---------------------------------------------------------------- RMSNorm
+
+def _rows(x: torch.Tensor, N: int, name: str) -> int:
+    if x.shape[-1] != N:
+        raise ValueError(f"{name}: last dim {x.shape[-1]} != normalized size {N}")
+    if not x.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return x.numel() // N if N else 0
+
+
+def rmsnorm_fwd(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, *,
+                out: torch.Tensor | None = None, rstd: torch.Tensor | None = None,
+                save_rstd: bool = True):
+    """y = bf16((x * rstd) * w), rstd = 1/sqrt(mean(x^2)+eps) per row (fp32).
+
+    Returns (y, rstd) with y shaped like x and rstd shaped x.shape[:-1]
+    (None when save_rstd is False)."""
+    _need(x, "x", torch.bfloat16)
+    _need(weight, "weight", torch.bfloat16, x.device)
+    N = weight.numel()
+    M = _rows(x, N, "x")
+    y = torch.empty_like(x) if out is None else out
+    if save_rstd and rstd is None:
+        rstd = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    with _on_device(x.device):
+        _lib.call("frag_rmsnorm_fwd", _ptr(x), _ptr(weight.contiguous()), _ptr(y),
+                  _ptr(rstd if save_rstd else None), M, N, float(eps), _stream(x.device))
+    return y, (rstd if save_rstd else None)
+
+
+def add_rmsnorm_fwd(residual: torch.Tensor, x: torch.Tensor, weight: torch.Tensor,
+                    eps: float = 1e-5, *, write_h: bool = True, save_rstd: bool = True,
+                    h_out: torch.Tensor | None = None, y_out: torch.Tensor | None = None):
+    """h = bf16(residual + x); y = rmsnorm(h) * w.  Returns (h, y, rstd)."""
+    _need(residual, "residual", torch.bfloat16)
+    _need(x, "x", torch.bfloat16, residual.device)
+    _need(weight, "weight", torch.bfloat16, residual.device)
+    if residual.shape != x.shape:
+        raise ValueError(f"residual {tuple(residual.shape)} and x {tuple(x.shape)} differ")
+    N = weight.numel()
+    M = _rows(x, N, "x")
+    _rows(residual, N, "residual")
+    h = (torch.empty_like(x) if h_out is None else h_out) if write_h else None
+    y = torch.empty_like(x) if y_out is None else y_out
+    rstd = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device) if save_rstd else None
+    with _on_device(x.device):
+        _lib.call("frag_add_rmsnorm_fwd", _ptr(residual), _ptr(x), _ptr(weight.contiguous()),
+                  _ptr(h), _ptr(y), _ptr(rstd), M, N, float(eps), _stream(x.device))
+    return h, y, rstd
+
+
+def rmsnorm_bwd_workspace_bytes(M: int, N: int, device=None) -> int:
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with _on_device(dev):
+        return int(_lib.load().frag_rmsnorm_bwd_workspace_bytes(M, N))
+
+
+def rmsnorm_bwd_num_blocks(M: int, N: int, device=None) -> int:
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with _on_device(dev):
+        return int(_lib.load().frag_rmsnorm_bwd_num_blocks(M, N))
+
+
+def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,
+                weight: torch.Tensor, *, dy2: torch.Tensor | None = None,
+                dres: torch.Tensor | None = None, eps: float = 1e-6,
+                dw_dtype: torch.dtype | None = torch.float32,
+                workspace: torch.Tensor | None = None, return_partials: bool = False):
+    """RMSNorm backward.  Returns (dx, dw[, partials]).
+
+    dy2   optional second gradient summed (in bf16) into dy first
+    rstd  saved rstd (fp32, one per row) or None to recompute it with eps
+    dres  optional residual gradient added (in bf16) to dx
+    dw    fp32 (dw_dtype=torch.float32), bf16, or None (not reduced)
+    partials  the [G, N] fp32 per-row-block sums, for cross-rank reductions
+    """
+    _need(dy, "dy", torch.bfloat16)
+    dev = dy.device
+    _need(x, "x", torch.bfloat16, dev)
+    _need(weight, "weight", torch.bfloat16, dev)
+    N = weight.numel()
+    M = _rows(x, N, "x")
+    if dy.shape != x.shape:
+        raise ValueError(f"dy {tuple(dy.shape)} and x {tuple(x.shape)} differ")
+    _rows(dy, N, "dy")
+    for name, t in (("dy2", dy2), ("dres", dres)):
+        if t is not None:
+            _need(t, name, torch.bfloat16, dev)
+            if t.shape != x.shape:
+                raise ValueError(f"{name} {tuple(t.shape)} and x {tuple(x.shape)} differ")
+            _rows(t, N, name)
+    if rstd is not None:
+        _need(rstd, "rstd", torch.float32, dev)
+        if rstd.numel() != M or not rstd.is_contiguous():
+            raise ValueError(f"rstd must be contiguous with {M} elements")
+    dx = torch.empty_like(x)
+    dw = None
+    if dw_dtype is not None:
+        if dw_dtype not in (torch.float32, torch.bfloat16):
+            raise TypeError("dw_dtype must be float32, bfloat16 or None")
+        dw = torch.empty(N, dtype=dw_dtype, device=dev)
+    with _on_device(dev):
+        lib = _lib.load()
+        need = int(lib.frag_rmsnorm_bwd_workspace_bytes(M, N))
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+        _lib.call("frag_rmsnorm_bwd", _ptr(dy), _ptr(dy2), _ptr(x), _ptr(rstd), _ptr(weight.contiguous()),
+                  _ptr(dres), _ptr(dx),
+                  _ptr(dw) if dw_dtype == torch.float32 else None,
+                  _ptr(dw) if dw_dtype == torch.bfloat16 else None,
+                  M, N, float(eps), _ptr(workspace), workspace.numel(), _stream(dev))
+        if return_partials:
+            G = int(lib.frag_rmsnorm_bwd_num_blocks(M, N)) if M else 0
+            parts = workspace[: G * N * 4].view(torch.float32).view(G, N)
+            return dx, dw, parts
+    return dx, dw
+
+
+def dw_reduce(partials: torch.Tensor, *, out: torch.Tensor | None = None,
+              out_bf16: torch.Tensor | None = None) -> torch.Tensor:
+    """Fixed-order sum over the rows of a [G, N] fp32 tensor."""
+    _need(partials, "partials", torch.float32)
+    if partials.dim() != 2 or not partials.is_contiguous():
+        raise ValueError("partials must be a contiguous [G, N] tensor")
+    G, N = partials.shape
+    if out is None and out_bf16 is None:
+        out = torch.empty(N, dtype=torch.float32, device=partials.device)
+    with _on_device(partials.device):
+        _lib.call("frag_dw_reduce", _ptr(partials), G, N, _ptr(out), _ptr(out_bf16),
+                  _stream(partials.device))
+    return out if out is not None else out_bf16
+
+
+# -------------------------------------------------------------- embedding
+
+def embedding_fwd(ids: torch.Tensor, table: torch.Tensor, *, vocab_lo: int = 0,
+                  vocab_total: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[..., :] = table[ids - vocab_lo] for ids in the shard, zero otherwise.
+
+    table is the whole table (vocab_lo=0) or one contiguous vocab shard
+    [vocab_lo, vocab_lo + table.shape[0]) of a vocab_total-row table."""
+    _need(ids, "ids", torch.int64)
+    _need(table, "table", torch.bfloat16, ids.device)
+    if table.dim() != 2 or not table.is_contiguous():
+        raise ValueError("table must be a contiguous [rows, D] tensor")
+    rows, D = table.shape
+    total = rows if vocab_total is None else int(vocab_total)
+    ids_c = ids.contiguous()
+    T = ids_c.numel()
+    o = torch.empty(*ids.shape, D, dtype=torch.bfloat16, device=ids.device) if out is None else out
+    with _on_device(ids.device):
+        st = _status_word(ids.device)
+        _lib.call("frag_embedding_fwd", _ptr(ids_c), _ptr(table), _ptr(o), T, rows, D,
+                  int(vocab_lo), total, _ptr(st), _stream(ids.device))
+    if _SYNC_CHECK:
+        check_status(ids.device)
+    return o
+
+
+def embedding_bwd(grad: torch.Tensor, ids: torch.Tensor, num_rows: int, *, vocab_lo: int = 0,
+                  vocab_total: int | None = None, padding_idx: int = -1,
+                  out: torch.Tensor | None = None,
+                  workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 table gradient G[v] = sum over tokens t (in order) with ids[t] == v of grad[t].
+
+    Every row of G is written (no memset needed).  num_rows is the number of
+    table rows this call owns (the whole vocab, or one shard at vocab_lo)."""
+    _need(grad, "grad", torch.bfloat16)
+    _need(ids, "ids", torch.int64, grad.device)
+    D = grad.shape[-1]
+    ids_c = ids.contiguous()
+    T = ids_c.numel()
+    if grad.numel() != T * D:
+        raise ValueError(f"grad {tuple(grad.shape)} does not match {T} ids x {D}")
+    g = grad.contiguous()
+    total = int(num_rows) if vocab_total is None else int(vocab_total)
+    G = torch.empty(num_rows, D, dtype=torch.float32, device=grad.device) if out is None else out
+    with _on_device(grad.device):
+        lib = _lib.load()
+        need = int(lib.frag_embedding_bwd_workspace_bytes(T, num_rows))
+        if need == 0 and num_rows > 0:
+            raise FragError("frag_embedding_bwd_workspace_bytes", 2, "unsupported sizes")
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=grad.device)
+        st = _status_word(grad.device)
+        _lib.call("frag_embedding_bwd", _ptr(ids_c), _ptr(g), _ptr(G), T, int(num_rows), D,
+                  int(vocab_lo), total, int(padding_idx), _ptr(workspace), workspace.numel(),
+                  _ptr(st), _stream(grad.device))
+    if _SYNC_CHECK:
+        check_status(grad.device)
+    return G
+
+
+# ------------------------------------------------------------------- RoPE
+
+_LAYOUTS = {"neox": _lib.FRAG_ROPE_NEOX, "interleaved": _lib.FRAG_ROPE_INTERLEAVED}
+
+
+def _rope_desc(x: torch.Tensor, out: torch.Tensor, name: str) -> _lib.RopeTensor:
+    if x.dim() != 4:
+        raise ValueError(f"{name} must be [B, S, H, D] (any strides, last dim contiguous)")
+    if x.stride(-1) != 1 or out.stride(-1) != 1:
+        raise ValueError(f"{name}: the head dimension must be contiguous")
+    if out.shape != x.shape:
+        raise ValueError(f"{name}: output shape {tuple(out.shape)} != {tuple(x.shape)}")
+    B, S, H, D = x.shape
+    return _lib.RopeTensor(x.data_ptr(), out.data_ptr(), H, x.stride(0), x.stride(1), x.stride(2),
+                           out.stride(0), out.stride(1), out.stride(2))
+
+
+def rope(q: torch.Tensor, k: torch.Tensor | None = None, positions: torch.Tensor | None = None, *,
+         theta: float | None = 500000.0, freqs: torch.Tensor | None = None,
+         layout: str = "neox", inverse: bool = False, out_q: torch.Tensor | None = None,
+         out_k: torch.Tensor | None = None):
+    """Rotary embedding of q (and k) given as [B, S, H, D] views (any strides,
+    contiguous head dim).  Returns (out_q, out_k); outputs default to new
+    contiguous tensors and may alias the inputs (in-place).
+
+    positions: int32/int64 [B, S] (or [S], broadcast over B), or None for
+    position = s.  freqs: complex64 [P, D/2] table indexed by position (the
+    reference's freqs_cis input); without it cos/sin are computed in
+    registers from theta.  inverse=True applies the conjugate rotation (the
+    backward)."""
+    _need(q, "q", torch.bfloat16)
+    dev = q.device
+    if layout not in _LAYOUTS:
+        raise ValueError(f"layout must be one of {sorted(_LAYOUTS)}")
+    B, S, Hq, D = q.shape
+    oq = torch.empty(q.shape, dtype=q.dtype, device=dev) if out_q is None else out_q
+    descs = [_rope_desc(q, oq, "q")]
+    ok = None
+    if k is not None:
+        _need(k, "k", torch.bfloat16, dev)
+        if k.shape[0] != B or k.shape[1] != S or k.shape[3] != D:
+            raise ValueError(f"k {tuple(k.shape)} does not match q {tuple(q.shape)}")
+        ok = torch.empty(k.shape, dtype=k.dtype, device=dev) if out_k is None else out_k
+        descs.append(_rope_desc(k, ok, "k"))
+    arr = (_lib.RopeTensor * len(descs))(*descs)
+    pos_ptr, pos_dtype, psb, pss = None, _lib.FRAG_POS_NONE, 0, 0
+    if positions is not None:
+        if positions.device != dev:
+            raise ValueError("positions must be on the same device as q")
+        if positions.dtype == torch.int64:
+            pos_dtype = _lib.FRAG_POS_I64
+        elif positions.dtype == torch.int32:
+            pos_dtype = _lib.FRAG_POS_I32
+        else:
+            raise TypeError("positions must be int32 or int64")
+        if positions.dim() == 1:
+            if positions.shape[0] != S:
+                raise ValueError("1-D positions must have S entries")
+            psb, pss = 0, positions.stride(0)
+        elif positions.dim() == 2 and tuple(positions.shape) == (B, S):
+            psb, pss = positions.stride(0), positions.stride(1)
+        else:
+            raise ValueError(f"positions must be [B, S] or [S], got {tuple(positions.shape)}")
+        pos_ptr = C.c_void_p(positions.data_ptr())
+    fptr, fstride = None, 0
+    if freqs is not None:
+        if freqs.dtype != torch.complex64 or freqs.device != dev:
+            raise TypeError("freqs must be a complex64 tensor on q's device")
+        f2 = freqs.reshape(-1, freqs.shape[-1])
+        if f2.shape[-1] != D // 2 or f2.stride(-1) != 1:
+            raise ValueError(f"freqs rows must hold D/2={D // 2} contiguous complex values")
+        fptr, fstride = C.c_void_p(f2.data_ptr()), f2.stride(0)
+        theta_v = 0.0
+    else:
+        if theta is None:
+            raise ValueError("either theta or freqs is required")
+        theta_v = float(theta)
+    with _on_device(dev):
+        _lib.call("frag_rope", arr, len(descs), B, S, D, pos_ptr, pos_dtype, psb, pss, fptr,
+                  fstride, theta_v, _LAYOUTS[layout], int(bool(inverse)), _stream(dev))
+    return oq, ok

@@ -1,0 +1,66 @@
+"""Shared pytest setup: the `gpu` marker and tolerance helpers.
+
+Tolerances (from the benchmark's parity rules):
+  bf16 outputs    |a - b| <= 1e-2 + 1.6e-2 * |b|
+  fp32 rstd / dw  |a - b| <= 1e-4 * |b| (+ a small absolute floor for
+                  near-zero dweight columns, 1e-4 * rms of the column terms)
+  embedding fwd   bit exact
+"""
+import os
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+BF16_ATOL = 1e-2
+BF16_RTOL = 1.6e-2
+F32_RTOL = 1e-4
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200) and libfrag.so")
+    config.addinivalue_line("markers", "slow: full-size cases")
+
+
+def pytest_collection_modifyitems(config, items):
+    if torch.cuda.is_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device")
+    for it in items:
+        if "gpu" in it.keywords:
+            it.add_marker(skip)
+
+
+def assert_bf16_close(actual: torch.Tensor, expected: torch.Tensor, what: str = "",
+                      atol: float = BF16_ATOL, rtol: float = BF16_RTOL):
+    a = actual.detach().float().cpu()
+    e = expected.detach().float().cpu()
+    assert a.shape == e.shape, f"{what}: shape {tuple(a.shape)} != {tuple(e.shape)}"
+    err = (a - e).abs()
+    bound = atol + rtol * e.abs()
+    bad = err > bound
+    if bad.any():
+        i = int(torch.argmax((err - bound).flatten()))
+        raise AssertionError(
+            f"{what}: {int(bad.sum())} of {a.numel()} elements out of tolerance; worst at flat "
+            f"{i}: got {a.flatten()[i].item()} want {e.flatten()[i].item()}")
+
+
+def assert_f32_close(actual: torch.Tensor, expected: torch.Tensor, what: str = "",
+                     rtol: float = F32_RTOL, atol: float = 0.0):
+    a = actual.detach().double().cpu()
+    e = expected.detach().double().cpu()
+    assert a.shape == e.shape, f"{what}: shape {tuple(a.shape)} != {tuple(e.shape)}"
+    err = (a - e).abs()
+    bound = atol + rtol * e.abs()
+    bad = err > bound
+    if bad.any():
+        i = int(torch.argmax((err - bound).flatten()))
+        raise AssertionError(
+            f"{what}: {int(bad.sum())} of {a.numel()} out of rtol {rtol}; worst at flat {i}: "
+            f"got {a.flatten()[i].item()} want {e.flatten()[i].item()}")

@@ -1,0 +1,86 @@
+"""GPU parity: RoPE (neox and interleaved, computed and table cos/sin, forward
+and inverse, strided views) vs the CPU oracle."""
+import pytest
+import torch
+
+from conftest import assert_bf16_close
+from kernelproblems_b200 import configs as cf
+from kernelproblems_b200 import ops
+from oracle import fragments as ora
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def test_rope_neox_c3_fwd_bwd():
+    c = cf.C3
+    q = cf.randn((c.B, c.S, c.Hq, c.D), seed=40)
+    k = cf.randn((c.B, c.S, c.Hk, c.D), seed=41)
+    pos = cf.rope_positions(c)
+    oq, ok = ops.rope(q.to(DEV), k.to(DEV), pos.to(DEV), theta=c.theta)
+    assert_bf16_close(oq, ora.rope_neox(q, pos, c.theta), "q")
+    assert_bf16_close(ok, ora.rope_neox(k, pos, c.theta), "k")
+    gq = cf.randn((c.B, c.S, c.Hq, c.D), seed=42)
+    gk = cf.randn((c.B, c.S, c.Hk, c.D), seed=43)
+    dq, dk = ops.rope(gq.to(DEV), gk.to(DEV), pos.to(DEV), theta=c.theta, inverse=True)
+    assert_bf16_close(dq, ora.rope_neox(gq, pos, c.theta, inverse=True), "dq")
+    assert_bf16_close(dk, ora.rope_neox(gk, pos, c.theta, inverse=True), "dk")
+
+
+def test_rope_round_trip_full_size():
+    c = cf.C3
+    q = cf.randn((c.B, c.S, c.Hq, c.D), device=DEV, seed=44)
+    pos = cf.rope_positions(c, device=DEV)
+    oq, _ = ops.rope(q, None, pos, theta=c.theta)
+    back, _ = ops.rope(oq, None, pos, theta=c.theta, inverse=True)
+    # rotation then its inverse: identity up to two bf16 roundings
+    assert_bf16_close(back, q, "inverse(rope(q))", atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("layout", ["neox", "interleaved"])
+@pytest.mark.parametrize("B,S,H,D", [(1, 7, 3, 128), (2, 33, 5, 64), (1, 4, 2, 32), (1, 5, 4, 96), (1, 3, 2, 256)])
+def test_rope_shapes(layout, B, S, H, D):
+    x = cf.randn((B, S, H, D), seed=B * 100 + S)
+    pos = torch.randint(0, 5000, (B, S), generator=torch.Generator().manual_seed(S))
+    o, _ = ops.rope(x.to(DEV), None, pos.to(DEV), theta=10000.0, layout=layout)
+    if layout == "neox":
+        ref = ora.rope_neox(x, pos, 10000.0)
+    else:
+        ref = ora.rope_interleaved_theta(x, pos, 10000.0)
+    assert_bf16_close(o, ref, f"{layout} D={D}")
+
+
+def test_rope_interleaved_table_reference_fragment():
+    """v8/c8c60d8f7015: int32 positions index a random complex64 freqs table."""
+    S, Hq, Hk, D = 8192, 32, 8, 128
+    g = torch.Generator().manual_seed(50)
+    pos = torch.randint(0, 100, (1, S), generator=g, dtype=torch.int32)
+    freqs = torch.randn((S, D // 2), dtype=torch.complex64, generator=g)
+    q = cf.randn((1, S, Hq, D), seed=51)
+    k = cf.randn((1, S, Hk, D), seed=52)
+    oq, ok = ops.rope(q.to(DEV), k.to(DEV), pos.to(DEV), freqs=freqs.to(DEV), layout="interleaved")
+    f = freqs[pos.squeeze(0).long()].view(1, S, 1, D // 2)
+    assert_bf16_close(oq, ora.rope_interleaved(q, f), "q")
+    assert_bf16_close(ok, ora.rope_interleaved(k, f), "k")
+
+
+def test_rope_interleaved_table_strided_bwd_fragment():
+    """v7/bfe872e373e4: grad arrives as a [1, H, S, D] transposed view of [S, H, D]
+    storage; freqs indexed by token."""
+    S, H, D = 8192, 32, 128
+    g = torch.Generator().manual_seed(60)
+    store = cf.randn((S * H * D,), seed=61)
+    gv = store.as_strided((1, H, S, D), (S * H * D, D, H * D, 1))
+    freqs = torch.randn((1, S, 1, D // 2), dtype=torch.complex64, generator=g)
+    x = gv.transpose(1, 2)  # [1, S, H, D] view, strides (.., H*D, D, 1)
+    xd = store.to(DEV).as_strided((1, H, S, D), (S * H * D, D, H * D, 1)).transpose(1, 2)
+    o, _ = ops.rope(xd, None, None, freqs=freqs.to(DEV).reshape(S, D // 2), layout="interleaved")
+    assert_bf16_close(o, ora.rope_interleaved(x, freqs), "grad")
+
+
+def test_rope_in_place():
+    x = cf.randn((2, 16, 4, 128), seed=70)
+    pos = torch.arange(16)
+    xd = x.to(DEV)
+    ops.rope(xd, None, pos.to(DEV), theta=500000.0, out_q=xd)
+    assert_bf16_close(xd, ora.rope_neox(x, pos, 500000.0), "in place")
