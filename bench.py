@@ -1,0 +1,743 @@
+#!/usr/bin/env python
+"""Fragment-suite benchmark: achieved HBM GB/s and tokens/s on B200.
+
+One step = one pass of every hot-path fragment over its configuration's
+synthetic batch, in this order (each fragment's inputs were last touched a
+whole step — more than 17 GB of traffic — earlier, so every read is cold in
+the 126 MB L2 without an explicit flush):
+
+  C0F  RMSNorm fwd            x[4,2048,4096]
+  C2F  embedding fwd          ids[8,4096] over table[128256,4096]
+  C1B  RMSNorm bwd            x, grad[4,2048,4096]  (+ dweight exchange at N>1)
+  C3F  RoPE fwd (neox)        q[8,4096,32,128], k[8,4096,8,128]
+  C2B  embedding bwd          fp32 table gradient [128256,4096]
+  C3B  RoPE bwd               grad_q, grad_k
+  C4F  residual add + RMSNorm res, x[16,8192,8192]
+  C4B  its backward           dy, dh, h -> d_res, dweight (+ exchange at N>1)
+
+`value` = algorithmic bytes of the step on all ranks / max-over-ranks device
+time per step (CUDA events on the launching stream, per-fragment CUDA graphs).
+At N>1 every rank runs its own batch (weak scaling); the only collective in
+the step is the dweight exchange of C1B and C4B.  The vocab-parallel embedding
+(masked gather + NCCL all-reduce of the output) is `--workload emb_vp`.
+
+`--impl reference` times the reference's torch-eager CPU graph (restated in
+oracle/fragments.py) on a row sample of the same workload on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "achieved HBM GB/s (% of 8 TB/s) and tokens/s per fragment at 1/2/4/8 B200"
+UNIT = "GB/s"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+SUITE = ["C0F", "C2F", "C1B", "C3F", "C2B", "C3B", "C4F", "C4B"]
+DOMINANT = "C4B"  # largest share of the step; its main kernel is the roofline kernel
+
+
+# ------------------------------------------------------------------ helpers
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="suite",
+                    help="suite | emb_vp | one fragment of " + ",".join(SUITE))
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0,
+                    help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--ref-seconds", type=float, default=150.0,
+                    help="target wall time of the whole --impl reference run")
+    ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-graphs", action="store_true", help="launch eagerly instead of graph replay")
+    ap.add_argument("--rows-frac", type=float, default=1.0,
+                    help="scale every config's rows/tokens (profiling captures of a smaller case only)")
+    ap.add_argument("--json-out", default=None)
+    return ap.parse_args(argv)
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs: STREAM-style copy)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback 6.65 TB/s (earlier measurement on this pool)"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the roofline kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "roofline_traffic.json"
+    try:
+        d = json.loads(p.read_text())
+        return d
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, enabled: bool = True):
+        self.proc = None
+        self.path = None
+        if not enabled:
+            return
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", str(gpu_index), "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(f[1]), smax=float(f[2]), power=float(f[3]),
+                                 hw=f[5], hwt=f[6], swt=f[7], swp=f[8]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        pmax = max(r["power"] for r in rows)
+        load = [r for r in rows if r["power"] >= 0.5 * pmax] or rows
+        reasons = set()
+        for r in rows:
+            if r["hw"].lower().startswith("active"):
+                reasons.add("hw_slowdown")
+            if r["hwt"].lower().startswith("active"):
+                reasons.add("hw_thermal_slowdown")
+            if r["swt"].lower().startswith("active"):
+                reasons.add("sw_thermal_slowdown")
+            if r["swp"].lower().startswith("active"):
+                reasons.add("sw_power_cap")
+        return {"sm_mhz": statistics.median(r["sm"] for r in load),
+                "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows),
+                "power_w_max": pmax}
+
+
+def count_kernel_nodes(graph) -> int:
+    """Kernel nodes in a captured torch CUDA graph (our launches incl. CUB's)."""
+    try:
+        from cuda.bindings import driver as cu
+        g = cu.CUgraph(graph.raw_cuda_graph())
+        err, _, n = cu.cuGraphGetNodes(g, 0)
+        err, nodes, n = cu.cuGraphGetNodes(g, n)
+        k = 0
+        for nd in nodes[:n]:
+            err, t = cu.cuGraphNodeGetType(nd)
+            if t == cu.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
+                k += 1
+        return k
+    except Exception:
+        return -1
+
+
+# --------------------------------------------------------------- fragments
+
+class Frag:
+    """One fragment at its configuration on this rank: device-resident inputs,
+    preallocated outputs, and the list of launch stages."""
+
+    def __init__(self, name, desc, tokens, nbytes, stages, exchange=None, e2e=None,
+                 kernels=None):
+        self.name, self.desc, self.tokens, self.bytes = name, desc, tokens, nbytes
+        self.stages = stages          # [(label, callable)] local launches
+        self.exchange = exchange      # callable or None (NCCL, eager)
+        self.e2e = e2e                # callable(host_inputs) -> (h2d, d2h) via the public API
+        self.kernels = kernels or {}
+        self.graphs = []
+        self.kernel_nodes = 0
+
+    def capture(self, use_graphs: bool):
+        for _, fn in self.stages:  # warm: load modules, size workspaces
+            fn()
+        torch.cuda.synchronize()
+        self.graphs = []
+        if not use_graphs:
+            return
+        for label, fn in self.stages:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                fn()
+            self.graphs.append(g)
+            self.kernel_nodes += max(count_kernel_nodes(g), 0)
+        torch.cuda.synchronize()
+
+    def launch_stage(self, i):
+        if self.graphs:
+            self.graphs[i].replay()
+        else:
+            self.stages[i][1]()
+
+
+def scaled_configs(frac: float):
+    """The five configs with their row (token) dimension scaled by frac."""
+    from dataclasses import replace
+
+    from kernelproblems_b200 import configs as cf
+    if frac == 1.0:
+        return cf.C0, cf.C1, cf.C2, cf.C3, cf.C4
+
+    def rows(cfg):
+        m = max(1, int(round(cfg.M * frac)))
+        return replace(cfg, shape=(m, cfg.N))
+    c2 = replace(cf.C2, batch=(1, max(1, int(round(cf.C2.T * frac)))))
+    c3 = replace(cf.C3, B=max(1, int(round(cf.C3.B * frac))))
+    return rows(cf.C0), rows(cf.C1), c2, c3, rows(cf.C4)
+
+
+def build_suite(dev, world, rank, names, pg, frac=1.0):
+    """Build the requested fragments.  Each builder has its own scope, so the
+    launch closures never see another fragment's tensors."""
+    from kernelproblems_b200 import configs as cf
+    from kernelproblems_b200 import ops
+    seed0 = 1000 * rank
+    C0, C1, C2, C3, C4 = scaled_configs(frac)
+
+    def exchange_dw(dw_part, dw_out, parts_buf):
+        if world == 1:
+            return None
+
+        def ex():
+            dist.all_gather_into_tensor(parts_buf, dw_part, group=pg)
+            ops.dw_reduce(parts_buf, out=dw_out)
+        return ex
+
+    def mk_c0f():
+        c = C0
+        x = cf.randn(c.shape, device=dev, seed=seed0 + 1)
+        w = cf.rmsnorm_weight(c.N, device=dev, seed=seed0 + 2)
+        y = torch.empty_like(x)
+        r = torch.empty(c.shape[:-1], dtype=torch.float32, device=dev)
+        f = Frag("C0F", c.name, c.M, cf.bytes_rmsnorm_fwd(c.M, c.N),
+                 [("rmsnorm_fwd", lambda: ops.rmsnorm_fwd(x, w, c.eps, out=y, rstd=r))])
+        f.host = dict(x=x)
+        f.e2e = lambda h: _e2e_call(lambda xs: ops.rmsnorm_fwd(xs["x"], w, c.eps), h)
+        return f
+
+    def mk_rms_bwd(name, c, with_dres, s):
+        w = cf.rmsnorm_weight(c.N, device=dev, seed=seed0 + s)
+        x = cf.randn(c.shape, device=dev, seed=seed0 + s + 1)
+        g = cf.randn(c.shape, device=dev, seed=seed0 + s + 2)
+        dh = cf.randn(c.shape, device=dev, seed=seed0 + s + 3) if with_dres else None
+        _, r = ops.rmsnorm_fwd(x, w, c.eps)
+        ws = torch.empty(ops.rmsnorm_bwd_workspace_bytes(c.M, c.N), dtype=torch.uint8, device=dev)
+        G = ops.rmsnorm_bwd_num_blocks(c.M, c.N)
+        parts = ws[: G * c.N * 4].view(torch.float32).view(G, c.N)
+        dw = torch.empty(c.N, dtype=torch.float32, device=dev)
+        dwg = torch.empty(c.N, dtype=torch.float32, device=dev)
+        pbuf = torch.empty(world, c.N, dtype=torch.float32, device=dev)
+        nb = cf.bytes_add_rmsnorm_bwd(c.M, c.N) if with_dres else cf.bytes_rmsnorm_bwd(c.M, c.N)
+        f = Frag(name, c.name + (" bwd" if with_dres else ""), c.M, nb,
+                 [("rmsnorm_bwd_main", lambda: ops.rmsnorm_bwd(g, x, r, w, dres=dh, dw_dtype=None,
+                                                              workspace=ws)),
+                  ("dw_reduce", lambda: ops.dw_reduce(parts, out=dw))],
+                 exchange=exchange_dw(dw, dwg, pbuf))
+        f.host = dict(g=g, x=x, r=r) if dh is None else dict(g=g, x=x, r=r, dh=dh)
+        f.e2e = lambda h: _e2e_call(lambda xs: ops.rmsnorm_bwd(xs["g"], xs["x"], xs["r"], w,
+                                                               dres=xs.get("dh")), h)
+        return f
+
+    def mk_c2(which):
+        c = C2
+        ids = cf.embedding_ids(c, device=dev, seed=2 + rank)
+        if which == "C2F":
+            table = cf.randn((c.vocab, c.dim), std=0.02, device=dev, seed=seed0 + 7)
+            out = torch.empty(*c.batch, c.dim, dtype=torch.bfloat16, device=dev)
+            f = Frag("C2F", c.name + " fwd", c.T, cf.bytes_embedding_fwd(c.T, c.dim),
+                     [("embedding_fwd", lambda: ops.embedding_fwd(ids, table, out=out))])
+            f.host = dict(ids=ids)
+            f.e2e = lambda h: _e2e_call(lambda xs: ops.embedding_fwd(xs["ids"], table), h)
+            return f
+        gr = cf.randn((*c.batch, c.dim), device=dev, seed=seed0 + 8)
+        Gt = torch.empty(c.vocab, c.dim, dtype=torch.float32, device=dev)
+        wsb = torch.empty(max(16, ops._lib.load().frag_embedding_bwd_workspace_bytes(c.T, c.vocab)),
+                          dtype=torch.uint8, device=dev)
+        f = Frag("C2B", c.name + " bwd", c.T, cf.bytes_embedding_bwd(c.T, c.dim, c.vocab),
+                 [("embedding_bwd", lambda: ops.embedding_bwd(gr, ids, c.vocab, out=Gt, workspace=wsb))])
+        f.host = dict(g=gr, ids=ids)
+        f.e2e = lambda h: _e2e_call(lambda xs: ops.embedding_bwd(xs["g"], xs["ids"], c.vocab), h)
+        return f
+
+    def mk_c3(which):
+        c = C3
+        inv = which == "C3B"
+        s = 13 if inv else 11
+        pos = cf.rope_positions(c, device=dev)
+        q = cf.randn((c.B, c.S, c.Hq, c.D), device=dev, seed=seed0 + s)
+        k = cf.randn((c.B, c.S, c.Hk, c.D), device=dev, seed=seed0 + s + 1)
+        oq, ok = torch.empty_like(q), torch.empty_like(k)
+        f = Frag(which, c.name + (" bwd" if inv else " fwd"), c.T, cf.bytes_rope(c.T, c.Hq, c.Hk, c.D),
+                 [("rope", lambda: ops.rope(q, k, pos, theta=c.theta, inverse=inv, out_q=oq, out_k=ok))])
+        f.host = dict(q=q, k=k)
+        f.e2e = lambda h: _e2e_call(lambda xs: ops.rope(xs["q"], xs["k"], pos, theta=c.theta,
+                                                        inverse=inv), h)
+        return f
+
+    def mk_c4f():
+        c = C4
+        w = cf.rmsnorm_weight(c.N, device=dev, seed=seed0 + 20)
+        res = cf.randn(c.shape, device=dev, seed=seed0 + 21)
+        x = cf.randn(c.shape, device=dev, seed=seed0 + 22)
+        h = torch.empty_like(x)
+        y = torch.empty_like(x)
+        f = Frag("C4F", c.name + " fwd", c.M, cf.bytes_add_rmsnorm_fwd(c.M, c.N),
+                 [("add_rmsnorm_fwd", lambda: ops.add_rmsnorm_fwd(res, x, w, c.eps, h_out=h, y_out=y))])
+        f.host = dict(res=res, x=x)
+        f.e2e = lambda h_: _e2e_call(lambda xs: ops.add_rmsnorm_fwd(xs["res"], xs["x"], w, c.eps), h_)
+        return f
+
+    builders = {"C0F": mk_c0f, "C1B": lambda: mk_rms_bwd("C1B", C1, False, 3),
+                "C2F": lambda: mk_c2("C2F"), "C2B": lambda: mk_c2("C2B"),
+                "C3F": lambda: mk_c3("C3F"), "C3B": lambda: mk_c3("C3B"),
+                "C4F": mk_c4f, "C4B": lambda: mk_rms_bwd("C4B", C4, True, 23)}
+    return [builders[n]() for n in SUITE if n in names]
+
+
+def _e2e_call(fn, host):
+    """Copy `host` (pinned) inputs to the device, run the public API call, copy
+    every output tensor back into pinned memory.  Returns (h2d, d2h) bytes."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    xs = {k: v.to(dev, non_blocking=True) for k, v in host["in"].items()}
+    outs = fn(xs)
+    outs = outs if isinstance(outs, (tuple, list)) else (outs,)
+    h2d = sum(v.numel() * v.element_size() for v in host["in"].values())
+    d2h = 0
+    for i, o in enumerate(o for o in outs if isinstance(o, torch.Tensor)):
+        buf = host["out"].get(i)
+        if buf is None or buf.shape != o.shape or buf.dtype != o.dtype:
+            buf = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+            host["out"][i] = buf
+        buf.copy_(o, non_blocking=True)
+        d2h += o.numel() * o.element_size()
+    return h2d, d2h
+
+
+# ------------------------------------------------------------------ CPU arm
+
+def cpu_suite_sample(frac: float, names):
+    """Build the CPU sample: each fragment's config with rows (tokens) scaled
+    by `frac` (embedding: tokens and vocab).  Returns [(name, bytes, tokens, fn)]."""
+    from kernelproblems_b200 import configs as cf
+    from oracle import fragments as ora
+    out = []
+
+    def rows(M):
+        return max(1, int(round(M * frac)))
+    if "C0F" in names:
+        c = cf.C0
+        m = rows(c.M)
+        x = cf.randn((m, c.N), seed=1)
+        w = cf.rmsnorm_weight(c.N)
+        out.append(("C0F", cf.bytes_rmsnorm_fwd(m, c.N), m, lambda x=x, w=w, eps=c.eps: ora.rmsnorm_fwd(x, w, eps)))
+    if "C2F" in names or "C2B" in names:
+        c = cf.C2
+        t = rows(c.T)
+        V = max(1, int(round(c.vocab * frac)))
+        cs = cf.EmbeddingCfg("sample", (1, t), V, c.dim)
+        ids = cf.embedding_ids(cs).reshape(-1)
+        if "C2F" in names:
+            table = cf.randn((V, c.dim), std=0.02, seed=7)
+            out.append(("C2F", cf.bytes_embedding_fwd(t, c.dim), t,
+                        lambda ids=ids, table=table: ora.embedding_fwd(table, ids)))
+        if "C2B" in names:
+            g = cf.randn((t, c.dim), seed=8)
+            out.append(("C2B", cf.bytes_embedding_bwd(t, c.dim, V), t,
+                        lambda g=g, ids=ids, V=V: ora.embedding_bwd(g, ids, V)))
+    if "C1B" in names:
+        c = cf.C1
+        m = rows(c.M)
+        x = cf.randn((m, c.N), seed=3)
+        w = cf.rmsnorm_weight(c.N)
+        g = cf.randn((m, c.N), seed=5)
+        _, r = ora.rmsnorm_fwd(x, w, c.eps)
+        out.append(("C1B", cf.bytes_rmsnorm_bwd(m, c.N), m,
+                    lambda g=g, x=x, r=r, w=w: ora.rmsnorm_bwd(g, x, r, w)))
+    if "C3F" in names or "C3B" in names:
+        c = cf.C3
+        s = max(1, int(round(c.S * frac * c.B)))
+        q = cf.randn((1, s, c.Hq, c.D), seed=11)
+        k = cf.randn((1, s, c.Hk, c.D), seed=12)
+        pos = torch.arange(s) % c.S
+        for nm, inv in (("C3F", False), ("C3B", True)):
+            if nm in names:
+                out.append((nm, cf.bytes_rope(s, c.Hq, c.Hk, c.D), s,
+                            lambda q=q, k=k, pos=pos, inv=inv, th=c.theta: (ora.rope_neox(q, pos, th, inv),
+                                                                       ora.rope_neox(k, pos, th, inv))))
+    if "C4F" in names or "C4B" in names:
+        c = cf.C4
+        m = rows(c.M)
+        w = cf.rmsnorm_weight(c.N)
+        res = cf.randn((m, c.N), seed=21)
+        x = cf.randn((m, c.N), seed=22)
+        if "C4F" in names:
+            out.append(("C4F", cf.bytes_add_rmsnorm_fwd(m, c.N), m,
+                        lambda res=res, x=x, w=w, eps=c.eps: ora.add_rmsnorm_fwd(res, x, w, eps)))
+        if "C4B" in names:
+            h, _, r = ora.add_rmsnorm_fwd(res, x, w, c.eps)
+            dy = cf.randn((m, c.N), seed=24)
+            out.append(("C4B", cf.bytes_add_rmsnorm_bwd(m, c.N), m,
+                        lambda dy=dy, h=h, r=r, w=w, dh=x: ora.add_rmsnorm_bwd(dy, None, h, r, w, dh)))
+    order = {n: i for i, n in enumerate(SUITE)}
+    return sorted(out, key=lambda t: order[t[0]])
+
+
+def run_cpu_sample(sample, reps: int = 1):
+    t_tot, b_tot, per = 0.0, 0, {}
+    for name, nb, tok, fn in sample:
+        fn()  # warm
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        dt = (time.perf_counter() - t0) / reps
+        per[name] = {"s": dt, "GB/s": nb / dt / 1e9, "tokens/s": tok / dt}
+        t_tot += dt
+        b_tot += nb
+    return b_tot / t_tot / 1e9, t_tot, per
+
+
+def calibrate_cpu(names, target_s: float):
+    """Pick a row fraction whose suite sample takes about target_s on the CPU."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    f0 = 1.0 / 64
+    _, t0, _ = run_cpu_sample(cpu_suite_sample(f0, names))
+    f = min(1.0, max(1.0 / 4096, f0 * target_s / max(t0, 1e-6)))
+    return f
+
+
+def cpu_baseline(names, target_s: float):
+    frac = calibrate_cpu(names, target_s / 2)
+    sample = cpu_suite_sample(frac, names)
+    gbs, t, per = run_cpu_sample(sample)
+    return {"value": round(gbs, 3), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": (f"torch-eager CPU restatement of the reference graphs (oracle/fragments.py), "
+                       f"each fragment on {frac:.4g} of its config's rows (embedding: tokens and vocab), "
+                       f"{t:.1f} s"),
+            "fragments": {k: {"GB/s": round(v["GB/s"], 3)} for k, v in per.items()}}
+
+
+# ---------------------------------------------------------------- main arms
+
+def config_dict(workload, world, l2_note):
+    from kernelproblems_b200 import configs as cf
+    return {"workload": workload,
+            "fragments": {"C0F": cf.C0.name, "C1B": cf.C1.name, "C2F": cf.C2.name + " fwd",
+                          "C2B": cf.C2.name + " bwd fp32 table", "C3F": cf.C3.name + " fwd",
+                          "C3B": cf.C3.name + " bwd", "C4F": cf.C4.name + " fwd",
+                          "C4B": cf.C4.name + " bwd"},
+            "parallelism": f"dp{world} (rows per rank fixed; dweight exchange for C1B/C4B)",
+            "l2": l2_note}
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    names = SUITE if args.workload == "suite" else [args.workload]
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    per_step = args.ref_seconds / (steps + warm + 2)
+    frac = calibrate_cpu(names, per_step)
+    sample = cpu_suite_sample(frac, names)
+    for _ in range(warm):
+        for _, _, _, fn in sample:
+            fn()
+    t0 = time.perf_counter()
+    tot_b = 0
+    for _ in range(steps):
+        for _, nb, _, fn in sample:
+            fn()
+            tot_b += nb
+    dt = time.perf_counter() - t0
+    gbs = tot_b / dt / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": UNIT,
+            "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": config_dict(args.workload, 1, "n/a (CPU)"),
+            "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": torch.get_num_threads(),
+                             "kind": "port",
+                             "sample": (f"torch-eager CPU restatement of the reference graphs "
+                                        f"(oracle/fragments.py) on {frac:.4g} of each config's rows "
+                                        f"per step")},
+            "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def ours_arm(args, rank, local_rank, world):
+    from kernelproblems_b200 import _lib
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    pg = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        pg = dist.group.WORLD
+    _lib.load()
+    if args.workload == "emb_vp":
+        return emb_vp_arm(args, rank, world, dev, pg)
+    names = SUITE if args.workload == "suite" else [args.workload]
+    frags = build_suite(dev, world, rank, names, pg, args.rows_frac)
+    for f in frags:
+        f.capture(not args.no_graphs)
+    step_bytes = sum(f.bytes for f in frags)
+    stream = torch.cuda.current_stream(dev)
+
+    def one_step(evs=None):
+        for fi, f in enumerate(frags):
+            if evs is not None:
+                evs[fi][0].record(stream)
+            for si in range(len(f.stages)):
+                f.launch_stage(si)
+                if evs is not None:
+                    evs[fi][1 + si].record(stream)
+            if f.exchange is not None:
+                f.exchange()
+            if evs is not None:
+                evs[fi][-1].record(stream)
+
+    for _ in range(max(3, args.warmup)):
+        one_step()
+    torch.cuda.synchronize()
+    K = args.steps
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(len(f.stages) + 2)] for f in frags]
+           for _ in range(K)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local_rank, enabled=(rank == 0 and not args.no_clocks))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start.record(stream)
+    for k in range(K):
+        one_step(evs[k])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    total_ms = t_start.elapsed_time(t_end)
+    frag_ms = {f.name: [] for f in frags}
+    stage_ms = {f.name: [[] for _ in f.stages] for f in frags}
+    for k in range(K):
+        for fi, f in enumerate(frags):
+            e = evs[k][fi]
+            frag_ms[f.name].append(e[0].elapsed_time(e[-1]))
+            prev = e[0]
+            for si in range(len(f.stages)):
+                stage_ms[f.name][si].append(prev.elapsed_time(e[1 + si]))
+                prev = e[1 + si]
+    # max over ranks
+    tmax = torch.tensor([total_ms] + [statistics.fmean(frag_ms[f.name]) for f in frags],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    tmax = tmax.tolist()
+    ms_step = tmax[0] / K
+    value = world * step_bytes / (ms_step * 1e-3) / 1e9
+    tokens = sum(f.tokens for f in frags)
+    peak, peak_note = measured_peak()
+
+    fr = {}
+    for i, f in enumerate(frags):
+        ms = tmax[1 + i]
+        fr[f.name] = {"ms": round(ms, 4), "GB/s_per_gpu": round(f.bytes / (ms * 1e-3) / 1e9, 1),
+                      "pct_of_8TBs": round(100 * f.bytes / (ms * 1e-3) / 1e9 / NOMINAL_HBM_GBS, 1),
+                      "frac_of_measured": round(f.bytes / (ms * 1e-3) / 1e9 / peak, 3),
+                      "tokens_per_s": round(world * f.tokens / (ms * 1e-3)),
+                      "bytes": f.bytes, "tokens": f.tokens, "kernels": f.kernel_nodes,
+                      "stages_ms": {lab: round(statistics.fmean(stage_ms[f.name][si]), 4)
+                                    for si, (lab, _) in enumerate(f.stages)}}
+    roof = None
+    dom = next((f for f in frags if f.name == DOMINANT), frags[0])
+    main_ms = statistics.fmean(stage_ms[dom.name][0])
+    achieved = dom.bytes / (main_ms * 1e-3) / 1e9
+    traffic = None
+    tinfo = profile_traffic()
+    if tinfo and tinfo.get("fragment") == dom.name:
+        traffic = tinfo.get("dram_bytes_per_launch")
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "kernel": f"{dom.name} {dom.stages[0][0]} (main kernel of the fragment)",
+            "algorithmic_bytes_per_launch": dom.bytes, "launch_ms": round(main_ms, 4),
+            "peak_source": peak_note, "pct_of_8TBs": round(100 * achieved / NOMINAL_HBM_GBS, 1)}
+
+    launches = sum(f.kernel_nodes for f in frags) * K if not args.no_graphs else None
+    line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": K, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded generators with the configs' shapes and distributions)",
+            "config": config_dict(args.workload, world,
+                                  "inputs larger than L2 across a step: each fragment's inputs were last "
+                                  "touched one step (>17 GB of traffic) earlier; no explicit flush"),
+            "pct_of_8TBs_per_gpu": round(100 * value / world / NOMINAL_HBM_GBS, 1),
+            "frac_of_measured_per_gpu": round(value / world / peak, 3),
+            "tokens_per_s_sum_over_fragments": round(world * tokens / (ms_step * 1e-3)),
+            "fragments": fr, "roofline": roof, "clocks": clk, "gpu_launches": launches}
+
+    # e2e through the public API with host buffers (every step: H2D inputs, D2H outputs)
+    if not args.no_e2e:
+        line["e2e"] = e2e_measure(frags, args.e2e_steps, world, dev, step_bytes)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(names, args.cpu_seconds)
+    for f in frags:
+        f.graphs = []
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+        if args.json_out:
+            Path(args.json_out).write_text(json.dumps(line, indent=1))
+    return 0
+
+
+def e2e_measure(frags, steps, world, dev, step_bytes):
+    hosts = {}
+    for f in frags:
+        hosts[f.name] = {"in": {k: v.detach().cpu().pin_memory() for k, v in f.host.items()}, "out": {}}
+    stream = torch.cuda.current_stream(dev)
+    # warm-up (allocator, pinned output buffers)
+    for f in frags:
+        f.e2e(hosts[f.name])
+        if f.exchange is not None:
+            f.exchange()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    h2d = d2h = 0
+    a.record(stream)
+    for _ in range(steps):
+        h2d = d2h = 0
+        for f in frags:
+            i, o = f.e2e(hosts[f.name])
+            if f.exchange is not None:
+                f.exchange()
+            h2d += i
+            d2h += o
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    return {"value": round(world * step_bytes / (ms * 1e-3) / 1e9, 2), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
+            "steps": steps,
+            "path": "kernelproblems_b200.ops public API, inputs from pinned host memory, "
+                    "every output copied back to pinned host memory"}
+
+
+def emb_vp_arm(args, rank, world, dev, pg):
+    """Vocab-parallel embedding over the group: the table is split into `world`
+    contiguous vocab shards; fwd = masked gather + NCCL all-reduce of the
+    [32768, 4096] bf16 output; bwd = each rank's fp32 table-gradient shard."""
+    from kernelproblems_b200 import configs as cf
+    from kernelproblems_b200 import ops, sharding
+    c = cf.C2
+    sh = cf.shard_rows(c.vocab, world, rank)
+    ids = cf.embedding_ids(c, device=dev)
+    table = cf.randn((sh.n, c.dim), std=0.02, device=dev, seed=7 + rank)
+    g = cf.randn((*c.batch, c.dim), device=dev, seed=8)
+    Gs = torch.empty(sh.n, c.dim, dtype=torch.float32, device=dev)
+    ws = torch.empty(max(16, ops._lib.load().frag_embedding_bwd_workspace_bytes(c.T, sh.n)),
+                     dtype=torch.uint8, device=dev)
+    out = torch.empty(*c.batch, c.dim, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        ops.embedding_fwd(ids, table, vocab_lo=sh.lo, vocab_total=c.vocab, out=out)
+        if world > 1:
+            dist.all_reduce(out, group=pg)
+        sharding.embedding_bwd_vocab_parallel(
+            g, ids, sh.lo, sh.n, c.vocab,
+            bwd_fn=lambda *a, **k: ops.embedding_bwd(*a, **k, out=Gs, workspace=ws))
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / args.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        dist.destroy_process_group()
+    ms = t.item()
+    nb = cf.bytes_embedding_fwd(c.T, c.dim) + cf.bytes_embedding_bwd(c.T, c.dim, c.vocab)
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "value": round(nb / (ms * 1e-3) / 1e9, 1), "unit": UNIT,
+                          "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+                          "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+                          "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+                          "tokens_per_s": round(c.T / (ms * 1e-3)),
+                          "config": {"workload": "emb_vp: vocab-parallel embedding fwd (masked gather + "
+                                                 "NCCL all-reduce) + bwd (fp32 shard gradient), C2 shapes",
+                                     "parallelism": f"vocab{world}"}}), flush=True)
+    return 0
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    rank, local_rank, world = env_rank()
+    if args.gpus != world and world == 1 and args.gpus > 1:
+        print(json.dumps({"error": f"--gpus {args.gpus} needs torchrun with {args.gpus} processes"}))
+        return 2
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    return ours_arm(args, rank, local_rank, world)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -151,9 +151,9 @@ int launch_fwd_t(const RowCfg& cfg, const uint16_t* x, const uint16_t* res,
 
 int launch_fwd(const void* res, const void* x, const void* w, void* h, void* y,
                float* rstd, int64_t M, int64_t N, float eps, cudaStream_t s) {
-  if (!x || !w || !y) return FRAG_ERR_INVALID_ARG;
   if (M < 0 || N < 0) return FRAG_ERR_INVALID_ARG;
   if (M == 0) return FRAG_OK;
+  if (!x || !w || !y) return FRAG_ERR_INVALID_ARG;
   if (N == 0 || M > 0x7fffffffLL) return FRAG_ERR_SHAPE;
   bool aligned = aligned16(x) && aligned16(w) && aligned16(y);
   if (res) aligned = aligned && aligned16(res);
@@ -490,7 +490,7 @@ int frag_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int64_t
 int frag_add_rmsnorm_fwd(const void* res, const void* x, const void* w, void* h, void* y,
                          float* rstd, int64_t M, int64_t N, float eps,
                          frag_stream_t stream) {
-  if (!res) return FRAG_ERR_INVALID_ARG;
+  if (!res && M > 0) return FRAG_ERR_INVALID_ARG;
   return launch_fwd(res, x, w, h, y, rstd, M, N, eps, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -520,9 +520,9 @@ int frag_rmsnorm_bwd(const void* dy, const void* dy2, const void* x, const float
                      const void* w, const void* dres, void* dx_out, float* dw, void* dw_bf16,
                      int64_t M, int64_t N, float eps, void* workspace,
                      size_t workspace_bytes, frag_stream_t stream) {
-  if (!dy || !x || !w || !dx_out) return FRAG_ERR_INVALID_ARG;
   if (M < 0 || N < 0) return FRAG_ERR_INVALID_ARG;
   if (N == 0 && M > 0) return FRAG_ERR_SHAPE;
+  if (M > 0 && (!dy || !x || !w || !dx_out)) return FRAG_ERR_INVALID_ARG;
   if (M > 0x7fffffffLL || N > 0x7fffffffLL) return FRAG_ERR_SHAPE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (M == 0) {

@@ -123,8 +123,9 @@ def rmsnorm_fwd(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, *,
     y = torch.empty_like(x) if out is None else out
     if save_rstd and rstd is None:
         rstd = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    wc = weight.contiguous()
     with _on_device(x.device):
-        _lib.call("frag_rmsnorm_fwd", _ptr(x), _ptr(weight.contiguous()), _ptr(y),
+        _lib.call("frag_rmsnorm_fwd", _ptr(x), _ptr(wc), _ptr(y),
                   _ptr(rstd if save_rstd else None), M, N, float(eps), _stream(x.device))
     return y, (rstd if save_rstd else None)
 
@@ -144,8 +145,9 @@ def add_rmsnorm_fwd(residual: torch.Tensor, x: torch.Tensor, weight: torch.Tenso
     h = (torch.empty_like(x) if h_out is None else h_out) if write_h else None
     y = torch.empty_like(x) if y_out is None else y_out
     rstd = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device) if save_rstd else None
+    wc = weight.contiguous()
     with _on_device(x.device):
-        _lib.call("frag_add_rmsnorm_fwd", _ptr(residual), _ptr(x), _ptr(weight.contiguous()),
+        _lib.call("frag_add_rmsnorm_fwd", _ptr(residual), _ptr(x), _ptr(wc),
                   _ptr(h), _ptr(y), _ptr(rstd), M, N, float(eps), _stream(x.device))
     return h, y, rstd
 
@@ -205,7 +207,8 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,
         need = int(lib.frag_rmsnorm_bwd_workspace_bytes(M, N))
         if workspace is None or workspace.numel() < need:
             workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
-        _lib.call("frag_rmsnorm_bwd", _ptr(dy), _ptr(dy2), _ptr(x), _ptr(rstd), _ptr(weight.contiguous()),
+        wc = weight.contiguous()
+        _lib.call("frag_rmsnorm_bwd", _ptr(dy), _ptr(dy2), _ptr(x), _ptr(rstd), _ptr(wc),
                   _ptr(dres), _ptr(dx),
                   _ptr(dw) if dw_dtype == torch.float32 else None,
                   _ptr(dw) if dw_dtype == torch.bfloat16 else None,

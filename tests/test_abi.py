@@ -1,0 +1,79 @@
+"""CPU checks of the C ABI: libfrag.so loads without a GPU, exports every
+entry point include/frag.h declares, and rejects bad arguments on the host
+(these calls return before touching CUDA)."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from kernelproblems_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "frag.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"FRAG_API\s+[\w\s\*]+?\b(frag_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert "frag_rmsnorm_fwd" in names and "frag_embedding_bwd" in names and "frag_rope" in names
+    assert len(names) >= 14
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"libfrag.so does not export {name}"
+
+
+def test_bindings_cover_header():
+    assert set(declared_symbols()) == set(_lib.SIGNATURES), \
+        "ctypes signatures and include/frag.h disagree"
+
+
+def test_version_and_status_strings():
+    assert "sm_100a" in _lib.version()
+    lib = _lib.load()
+    for code in range(7):
+        assert lib.frag_status_string(code)
+    assert b"unknown" in lib.frag_status_string(99)
+
+
+def test_invalid_arguments_rejected_on_host():
+    lib = _lib.load()
+    null = None
+    assert lib.frag_rmsnorm_fwd(null, null, null, null, 4, 8, 1e-5, null) == 1
+    assert lib.frag_rmsnorm_fwd(null, null, null, null, -1, 8, 1e-5, null) == 1
+    assert lib.frag_rmsnorm_fwd(null, null, null, null, 0, 8, 1e-5, null) == 0  # empty: no work
+    assert lib.frag_add_rmsnorm_fwd(null, null, null, null, null, null, 4, 8, 1e-5, null) == 1
+    assert lib.frag_rmsnorm_bwd(null, null, null, null, null, null, null, null, null, 4, 8, 1e-5,
+                                null, 0, null) == 1
+    assert lib.frag_rmsnorm_bwd(null, null, null, null, null, null, null, null, null, 0, 0, 1e-5,
+                                null, 0, null) == 0
+    assert lib.frag_embedding_fwd(null, null, null, -1, 4, 4, 0, 4, null, null) == 1
+    assert lib.frag_embedding_fwd(null, null, null, 0, 4, 4, 0, 4, null, null) == 0
+    assert lib.frag_embedding_bwd(null, null, null, -1, 4, 4, 0, 4, -1, null, 0, null, null) == 1
+    assert lib.frag_dw_reduce(null, 1, 4, null, null, null) == 1
+    assert lib.frag_rope(None, 1, 1, 1, 128, null, 0, 0, 0, null, 0, 1e4, 0, 0, null) == 1
+    t = (_lib.RopeTensor * 1)(_lib.RopeTensor(0, 0, 1, 0, 0, 0, 0, 0, 0))
+    assert lib.frag_rope(t, 1, 1, 1, 128, null, 0, 0, 0, null, 0, 1e4, 7, 0, null) == 1  # bad layout
+    assert lib.frag_rope(t, 3, 1, 1, 128, null, 0, 0, 0, null, 0, 1e4, 0, 0, null) == 1  # > 2 tensors
+    assert lib.frag_rope(t, 1, 1, 1, 127, null, 0, 0, 0, null, 0, 1e4, 0, 0, null) == 2  # odd D
+
+
+def test_fraggerror_message():
+    e = _lib.FragError("frag_x", 4)
+    assert "FRAG_ERR_WORKSPACE" in str(e) and e.status == 4
+
+
+def test_missing_library_fails_loudly(tmp_path, monkeypatch):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setenv("FRAG_LIBRARY", str(tmp_path / "nope.so"))
+    with pytest.raises(FileNotFoundError):
+        _lib.load()
+    monkeypatch.undo()
+    _lib._lib = None
+    _lib.load()

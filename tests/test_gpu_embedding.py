@@ -2,7 +2,7 @@
 import pytest
 import torch
 
-from conftest import assert_bf16_close, assert_f32_close
+from conftest import assert_f32_close
 from kernelproblems_b200 import configs as cf
 from kernelproblems_b200 import ops
 from oracle import fragments as ora
@@ -74,10 +74,11 @@ def test_embedding_bwd_c2():
     cnt = torch.bincount(ids.reshape(-1), minlength=c.vocab)[rows].double()
     atol = (1e-4 * cnt.sqrt()).unsqueeze(1)
     assert_f32_close(Gc[rows], ref[rows], "G", atol=atol)
-    # against the reference graph itself (it rounds each summed row to bf16)
-    eager = ora.embedding_bwd(grad[:1, :512], ids[:1, :512], c.vocab)
-    G_small = ops.embedding_bwd(grad[:1, :512].to(DEV), ids[:1, :512].to(DEV), c.vocab).cpu()
-    assert_bf16_close(G_small, eager, "G vs eager")
+    # Against the reference graph itself: its CPU kernel accumulates in bf16,
+    # so only rows hit by exactly one token are comparable, and those are exact.
+    single = rows[cnt == 1]
+    eager = ora.embedding_bwd(grad, ids, c.vocab)
+    assert torch.equal(Gc[single], eager[single]), "single-token rows must be exact copies"
 
 
 def test_embedding_bwd_deterministic_hot_ids():
