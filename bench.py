@@ -244,7 +244,7 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
             return None
 
         def ex():
-            dist.all_gather_into_tensor(parts_buf, dw_part, group=pg)
+            dist.all_gather_into_tensor(parts_buf.view(-1), dw_part, group=pg)
             ops.dw_reduce(parts_buf, out=dw_out)
         return ex
 

@@ -66,9 +66,9 @@ def _sum_over_ranks(dw: torch.Tensor, group, exact_order: bool,
     if not exact_order:
         dist.all_reduce(dw, op=dist.ReduceOp.SUM, group=group)
         return dw
-    parts = torch.empty(world, dw.numel(), dtype=dw.dtype, device=dw.device)
+    parts = torch.empty(world * dw.numel(), dtype=dw.dtype, device=dw.device)
     dist.all_gather_into_tensor(parts, dw.contiguous(), group=group)
-    return reduce_fn(parts)
+    return reduce_fn(parts.view(world, dw.numel()))
 
 
 def rmsnorm_bwd_dp(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,

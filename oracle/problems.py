@@ -1,0 +1,173 @@
+"""Per-problem oracle: each reference problem's Model.forward restated on the
+CPU with oracle.fragments.  TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).
+
+Every function takes the problem's inputs in get_inputs() order and returns
+the same output structure; tests/test_oracle_golden.py checks each one
+reproduces the reference Model's outputs bit for bit (sha256) on the seeded
+golden inputs.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import fragments as F
+
+aten = torch.ops.aten
+
+
+def rms_fwd_f4e9e58fef73(x, w):
+    """v8/f4e9e58fef73/problem.py:16-30."""
+    y, rstd = F.rmsnorm_fwd(x, w, 1e-5)
+    y2 = y.view(8192, 4096)
+    return (y2, y2, rstd)
+
+
+def rms_fwd_4b90e2d83144(x, w):
+    """v8/4b90e2d83144/problem.py:16-29."""
+    y, _ = F.rmsnorm_fwd(x, w, 1e-5)
+    y2 = y.view(8192, 4096)
+    return (y2, y2, y2)
+
+
+def rms_fwd_59f786beb25f(x, w):
+    """v7/59f786beb25f/problem.py:15-21."""
+    y, rstd = F.rmsnorm_fwd(x, w, 1e-5)
+    return (y, rstd)
+
+
+def _fsdp_weight(v):
+    # view.dtype -> clone(contiguous) -> _unsafe_view [4096] (v7/215dd2e6a519/problem.py:16-22)
+    return aten._unsafe_view.default(aten.clone.default(v, memory_format=torch.contiguous_format), [4096])
+
+
+def rms_fwd_215dd2e6a519(shard, x):
+    """v7/215dd2e6a519/problem.py:16-34."""
+    y, _ = F.rmsnorm_fwd(x, _fsdp_weight(shard), 1e-5)
+    y2 = y.view(8192, 4096)
+    return (y2, y2, y2)
+
+
+def rms_fwd_ac3fb0b7281f(shard, x):
+    """v7/ac3fb0b7281f/problem.py:16-31."""
+    y, _ = F.rmsnorm_fwd(x, _fsdp_weight(shard), 1e-5)
+    y2 = y.view(8192, 4096)
+    return (y2, y2)
+
+
+def add_rms_fwd_7884328a5557(mm_220, add_61, w):
+    """v8/7884328a5557/problem.py:17-33: add(add_61, mm_220) then _fused_rms_norm."""
+    _, y, _ = F.add_rmsnorm_fwd(add_61, aten._unsafe_view.default(mm_220, [1, 8192, 4096]), w, 1e-5)
+    y2 = y.view(8192, 4096)
+    return (y2, y2)
+
+
+def rms_bwd_45990c83cfd6(x, w, dy):
+    """v7/45990c83cfd6/problem.py:17-27."""
+    dx, dw = F.rmsnorm_recompute_bwd(x, w, dy, 1e-5)
+    return (dx, dw)
+
+
+def add_rms_bwd_7f544ceb2120(mm_666, view_1776, h, rstd, w, add_218):
+    """v7/7f544ceb2120/problem.py:20-38: dy = add(view_1776, mm_666)."""
+    dy = aten.add.Tensor(view_1776, aten.view.default(mm_666, [1, 8192, 4096]))
+    dx, dw = F.rmsnorm_bwd(dy, h, rstd, w)
+    return (aten.add.Tensor(add_218, dx), aten._to_copy.default(dw, dtype=torch.float32))
+
+
+def add_rms_bwd_d8f596b3df34(mm_664, mm_666, h, rstd, w, add_218):
+    """v8/d8f596b3df34/problem.py:23-46: dy = add(mm_664, mm_666)."""
+    dy = aten.add.Tensor(aten.view.default(mm_664, [1, 8192, 4096]),
+                         aten.view.default(mm_666, [1, 8192, 4096]))
+    dx, dw = F.rmsnorm_bwd(dy, h, rstd, w)
+    out = aten.add.Tensor(add_218, dx)
+    return (out.view(8192, 4096), aten._to_copy.default(dw, dtype=torch.float32))
+
+
+def emb_fwd_1e49beb8a123(flat, ids):
+    """v7/1e49beb8a123/problem.py:16-23."""
+    return F.embedding_fwd(flat.view(128256, 4096), ids)
+
+
+def emb_bwd_a12a160cb11b(grad, ids):
+    """v7/a12a160cb11b/problem.py:16-19."""
+    return F.embedding_bwd(grad, ids, 128256, -1)
+
+
+def _rope_rows(x2d, S, freqs_rows):
+    x = x2d.view(1, S, -1, 128)
+    return F.rope_interleaved(x, freqs_rows.view(1, S, 1, 64))
+
+
+def rope_c8c60d8f7015(pos, freqs, mm, mm_1):
+    """v8/c8c60d8f7015/problem.py:18-70: freqs_cis[pos] (index.Tensor)."""
+    f = aten.index.Tensor(freqs, [aten.squeeze.dim(pos, 0)])
+    return (_rope_rows(mm, 8192, f), _rope_rows(mm_1, 8192, f))
+
+
+def rope_97032595d968(mm, mm_1, pos, freqs):
+    """v8/97032595d968/problem.py (same graph, argument order mm, mm_1, pos, freqs)."""
+    return rope_c8c60d8f7015(pos, freqs, mm, mm_1)
+
+
+def rope_493cad38cac9(mm_217, view_788):
+    """v8/493cad38cac9/problem.py: q rows x freqs[1, S, 1, 64]."""
+    return _rope_rows(mm_217, 8192, view_788)
+
+
+def rope_e29b92927600(mm_218, view_788):
+    """v8/e29b92927600/problem.py:17-33."""
+    return _rope_rows(mm_218, 8192, view_788)
+
+
+def _rope_bwd(grad_bhsd, freqs):
+    # transpose.int(1, 2) -> _to_copy f32 -> complex mul -> bf16 -> view [S, H*D]
+    x = aten.transpose.int(grad_bhsd, 1, 2)
+    _, S, H, D = x.shape
+    return F.rope_interleaved(x, freqs).view(S, H * D)
+
+
+def rope_bwd_bfe872e373e4(g, freqs):
+    """v7/bfe872e373e4/problem.py:17-34."""
+    return _rope_bwd(g, freqs)
+
+
+def rope_bwd_5c65f62b0422(g, freqs):
+    """v7/5c65f62b0422/problem.py:17-34."""
+    return _rope_bwd(g, freqs)
+
+
+def rope_bwd_03d64c25b654(conj_freqs, g):
+    """v6/03d64c25b654/problem.py:12-43: clone(conj) then the same multiply."""
+    return _rope_bwd(g, aten.clone.default(conj_freqs))
+
+
+ORACLES = {
+    "v8/f4e9e58fef73": rms_fwd_f4e9e58fef73,
+    "v7/f4e9e58fef73": rms_fwd_f4e9e58fef73,
+    "v8/4b90e2d83144": rms_fwd_4b90e2d83144,
+    "v7/59f786beb25f": rms_fwd_59f786beb25f,
+    "v7/215dd2e6a519": rms_fwd_215dd2e6a519,
+    "v6/215dd2e6a519": rms_fwd_215dd2e6a519,
+    "v7/ac3fb0b7281f": rms_fwd_ac3fb0b7281f,
+    "v6/ac3fb0b7281f": rms_fwd_ac3fb0b7281f,
+    "v8/7884328a5557": add_rms_fwd_7884328a5557,
+    "v7/45990c83cfd6": rms_bwd_45990c83cfd6,
+    "v7/7f544ceb2120": add_rms_bwd_7f544ceb2120,
+    "v8/d8f596b3df34": add_rms_bwd_d8f596b3df34,
+    "v7/1e49beb8a123": emb_fwd_1e49beb8a123,
+    "v6/1e49beb8a123": emb_fwd_1e49beb8a123,
+    "v5/1e49beb8a123": emb_fwd_1e49beb8a123,
+    "v4/1e49beb8a123": emb_fwd_1e49beb8a123,
+    "v7/a12a160cb11b": emb_bwd_a12a160cb11b,
+    "v8/c8c60d8f7015": rope_c8c60d8f7015,
+    "v6/c8c60d8f7015": rope_c8c60d8f7015,
+    "v8/97032595d968": rope_97032595d968,
+    "v6/97032595d968": rope_97032595d968,
+    "v8/493cad38cac9": rope_493cad38cac9,
+    "v7/493cad38cac9": rope_493cad38cac9,
+    "v8/e29b92927600": rope_e29b92927600,
+    "v7/e29b92927600": rope_e29b92927600,
+    "v7/bfe872e373e4": rope_bwd_bfe872e373e4,
+    "v7/5c65f62b0422": rope_bwd_5c65f62b0422,
+    "v6/03d64c25b654": rope_bwd_03d64c25b654,
+}

@@ -1,0 +1,49 @@
+"""Regenerate a reference problem's inputs from a recorded spec.
+
+make_golden.py runs each reference ``get_inputs()`` with torch.randn /
+torch.randint replaced by seeded CPU generators and records, per returned
+input, how to rebuild it: the base tensor (kind, numel/shape, dtype, range,
+seed) and the view applied to it (shape, stride, storage offset).  This file
+replays those specs anywhere (no reference checkout needed), on any device.
+"""
+from __future__ import annotations
+
+import torch
+
+# bound at import, so replaying specs works while torch.randn is patched
+_randn = torch.randn
+_randint = torch.randint
+
+DTYPES = {
+    "bfloat16": torch.bfloat16,
+    "float32": torch.float32,
+    "complex64": torch.complex64,
+    "int64": torch.int64,
+    "int32": torch.int32,
+}
+
+
+def base_tensor(spec: dict) -> torch.Tensor:
+    """The seeded base tensor of one input, on the CPU."""
+    g = torch.Generator().manual_seed(int(spec["seed"]))
+    dt = DTYPES[spec["dtype"]]
+    size = tuple(spec["size"])
+    if spec["kind"] == "randn":
+        if dt == torch.complex64:
+            return _randn(size, dtype=torch.complex64, generator=g)
+        return _randn(size, dtype=torch.float32, generator=g).to(dt)
+    if spec["kind"] == "randint":
+        return _randint(int(spec["low"]), int(spec["high"]), size, dtype=dt, generator=g)
+    raise ValueError(f"unknown input kind {spec['kind']}")
+
+
+def make_input(spec: dict, device="cpu") -> torch.Tensor:
+    base = base_tensor(spec).to(device)
+    v = spec.get("view")
+    if v is None:
+        return base
+    return base.as_strided(tuple(v["shape"]), tuple(v["stride"]), int(v["offset"]))
+
+
+def make_inputs(specs: list[dict], device="cpu") -> list[torch.Tensor]:
+    return [make_input(s, device) for s in specs]

@@ -1,0 +1,155 @@
+"""Generate golden fixtures by running the reference problems themselves.
+
+Run in a checkout that has the reference next to it (not on the GPU box):
+
+    python tests/golden/make_golden.py --reference /path/to/KernelProblems
+
+For every registered problem ``vN/<hash>`` this loads the reference's own
+``problem.py``, patches its device literals to the CPU, draws its inputs by
+calling its ``get_inputs()`` with torch.randn / torch.randint replaced by
+seeded CPU generators (recording a replayable spec, see inputs.py), runs
+``Model().forward`` in torch eager on the CPU and writes
+``tests/golden/<vN>_<hash>.pt`` with the input specs and, per output, its
+shape/stride/dtype, the sha256 of its bytes, a float64 sum and a few sampled
+rows.  ``aten._fused_rms_norm_backward`` has no CPU kernel in torch 2.11, so
+the decomposition torch registers for it (torch/_decomp/decompositions.py:1862)
+is installed as its CPU kernel for the duration of the run.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import re
+import sys
+import types
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parent.parent))
+sys.path.insert(0, str(HERE))
+
+from inputs import base_tensor  # noqa: E402
+from kernelproblems_b200.problems import PROBLEMS  # noqa: E402
+
+SEED_BASE = 20260
+
+
+def sha256(t: torch.Tensor) -> str:
+    c = t.detach().contiguous().cpu()
+    if c.dtype == torch.complex64:
+        c = torch.view_as_real(c)
+    return hashlib.sha256(c.view(torch.uint8).numpy().tobytes()).hexdigest()
+
+
+def sample_rows(t: torch.Tensor) -> dict:
+    """Rows 0, 1, middle and last of the output flattened to 2-D."""
+    t2 = t.detach().reshape(-1, t.shape[-1]) if t.dim() > 1 else t.detach().reshape(1, -1)
+    idx = sorted({0, min(1, t2.shape[0] - 1), t2.shape[0] // 2, t2.shape[0] - 1})
+    return {"rows": idx, "values": t2[idx].clone()}
+
+
+def load_problem(ref_root: Path, key: str) -> types.ModuleType:
+    src = (ref_root / key / "problem.py").read_text()
+    src = src.replace("device(type='cuda', index=0)", "device(type='cpu')")
+    src = re.sub(r"device='cuda(:0)?'", "device='cpu'", src)
+    mod = types.ModuleType(key.replace("/", "_"))
+    exec(compile(src, str(ref_root / key / "problem.py"), "exec"), mod.__dict__)
+    return mod
+
+
+class SeededInputs:
+    """Context that makes torch.randn / torch.randint seeded, CPU, recorded."""
+
+    def __init__(self, seed0: int):
+        self.seed = seed0
+        self.records: list[dict] = []
+
+    def __enter__(self):
+        self._randn, self._randint = torch.randn, torch.randint
+        rec = self
+
+        def randn(*size, dtype=None, device=None, **kw):
+            size = tuple(size[0]) if len(size) == 1 and isinstance(size[0], (list, tuple)) else tuple(size)
+            spec = {"kind": "randn", "size": list(size), "dtype": str(dtype or torch.float32).split(".")[-1],
+                    "seed": rec.seed}
+            rec.seed += 1
+            t = base_tensor(spec)
+            rec.records.append({"spec": spec, "ptr": t.data_ptr()})
+            return t
+
+        def randint(low, high, size, dtype=None, device=None, **kw):
+            spec = {"kind": "randint", "size": list(size), "low": int(low), "high": int(high),
+                    "dtype": str(dtype or torch.int64).split(".")[-1], "seed": rec.seed}
+            rec.seed += 1
+            t = base_tensor(spec)
+            rec.records.append({"spec": spec, "ptr": t.data_ptr()})
+            return t
+
+        torch.randn, torch.randint = randn, randint
+        return self
+
+    def __exit__(self, *exc):
+        torch.randn, torch.randint = self._randn, self._randint
+
+    def spec_for(self, t: torch.Tensor) -> dict:
+        ptr = t.untyped_storage().data_ptr()
+        for r in self.records:
+            if r["ptr"] == ptr:
+                s = dict(r["spec"])
+                base_shape = tuple(s["size"])
+                if tuple(t.shape) != base_shape or t.stride() != torch.empty(base_shape).stride() \
+                        or t.storage_offset() != 0:
+                    s["view"] = {"shape": list(t.shape), "stride": list(t.stride()),
+                                 "offset": t.storage_offset()}
+                return s
+        raise RuntimeError("input not produced by randn/randint")
+
+
+def install_cpu_rms_backward():
+    from torch._decomp import decomposition_table
+    fn = decomposition_table[torch.ops.aten._fused_rms_norm_backward.default]
+    lib = torch.library.Library("aten", "IMPL")
+    lib.impl("_fused_rms_norm_backward", fn, "CPU")
+    return lib
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", default=None)
+    a = ap.parse_args(argv)
+    ref = Path(a.reference)
+    torch.manual_seed(0)
+    torch.set_num_threads(8)
+    keep = install_cpu_rms_backward()  # noqa: F841
+    for i, key in enumerate(sorted(PROBLEMS)):
+        if a.only and a.only not in key:
+            continue
+        mod = load_problem(ref, key)
+        with SeededInputs(SEED_BASE + 100 * i) as rec:
+            inputs = mod.get_inputs()
+        specs = [rec.spec_for(t) for t in inputs]
+        with torch.no_grad():
+            outs = mod.Model()(*inputs)
+        outs = outs if isinstance(outs, (tuple, list)) else (outs,)
+        desc = []
+        for o in outs:
+            desc.append({"shape": list(o.shape), "stride": list(o.stride()), "dtype": str(o.dtype).split(".")[-1],
+                         "sha256": sha256(o), "sum": float(o.double().sum()) if not o.is_complex() else None,
+                         "data_ptr_group": None, **sample_rows(o)})
+        # which outputs alias one buffer (views of the same tensor)
+        ptrs = [o.untyped_storage().data_ptr() for o in outs]
+        for d, p in zip(desc, ptrs):
+            d["data_ptr_group"] = ptrs.index(p)
+        fixture = {"problem": key, "torch": torch.__version__, "inputs": specs, "outputs": desc,
+                   "source": f"reference {key}/problem.py Model.forward on CPU (torch eager)"}
+        out = HERE / (key.replace("/", "_") + ".pt")
+        torch.save(fixture, out)
+        print(f"{key}: {len(specs)} inputs, {len(desc)} outputs -> {out.name} "
+              f"({out.stat().st_size // 1024} KiB)", flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,96 @@
+"""GPU parity of every drop-in kernel_function on the golden inputs.
+
+For each reference problem: the drop-in (libfrag.so through the C ABI) runs on
+the seeded golden inputs rebuilt on the GPU (same shapes and strides as the
+reference's get_inputs), and must match
+  * the output structure of the reference Model (count, shapes, dtypes, and
+    which outputs are views of one buffer),
+  * the pinned CPU oracle within the parity tolerances
+    (bf16 atol 1e-2 / rtol 1.6e-2, fp32 rstd rtol 1e-4, embedding bit exact),
+  * the golden rows the reference itself produced,
+and fp32 reductions (dweight, table gradient) must match a float64 sum within
+rtol 1e-4 (the reference graphs round those sums to bf16, see oracle)."""
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+from conftest import assert_bf16_close, assert_f32_close
+from kernelproblems_b200.problems import PROBLEMS
+from oracle import fragments as F
+from oracle.problems import ORACLES
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+sys.path.insert(0, str(GOLDEN))
+from inputs import make_inputs  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+FIXTURES = sorted(GOLDEN.glob("v*_*.pt"))
+
+EXACT = {"v7/1e49beb8a123", "v6/1e49beb8a123", "v5/1e49beb8a123", "v4/1e49beb8a123"}
+RMS_BWD = {"v7/45990c83cfd6", "v7/7f544ceb2120", "v8/d8f596b3df34"}
+EMB_BWD = {"v7/a12a160cb11b"}
+
+
+def _check_structure(outs, fx):
+    assert len(outs) == len(fx["outputs"]), "number of outputs"
+    ptrs = [o.untyped_storage().data_ptr() for o in outs]
+    for i, (o, ref) in enumerate(zip(outs, fx["outputs"])):
+        assert list(o.shape) == ref["shape"], f"output {i} shape {list(o.shape)} != {ref['shape']}"
+        assert str(o.dtype).split(".")[-1] == ref["dtype"], f"output {i} dtype"
+        assert o.is_cuda
+        assert ptrs.index(ptrs[i]) == ref["data_ptr_group"], f"output {i} aliasing differs"
+
+
+def _dw_f64(key, cpu_in):
+    if key == "v7/45990c83cfd6":
+        x, w, dy = cpu_in
+        _, rstd = F.rmsnorm_fwd(x, w, 1e-5)
+        return F.rmsnorm_dw_f64(dy, x, rstd), (dy, x, rstd)
+    if key == "v7/7f544ceb2120":
+        mm_666, view_1776, h, rstd, w, _ = cpu_in
+        dy = torch.ops.aten.add.Tensor(view_1776, mm_666.view(h.shape))
+    else:
+        mm_664, mm_666, h, rstd, w, _ = cpu_in
+        dy = torch.ops.aten.add.Tensor(mm_664.view(h.shape), mm_666.view(h.shape))
+    return F.rmsnorm_dw_f64(dy, h, rstd), (dy, h, rstd)
+
+
+@pytest.mark.parametrize("fixture", FIXTURES, ids=lambda p: p.stem)
+def test_problem_drop_in(fixture):
+    fx = torch.load(fixture, weights_only=False)
+    key = fx["problem"]
+    cpu_in = make_inputs(fx["inputs"])
+    gpu_in = make_inputs(fx["inputs"], device="cuda")
+    outs = PROBLEMS[key](*gpu_in)
+    outs = outs if isinstance(outs, (tuple, list)) else (outs,)
+    torch.cuda.synchronize()
+    _check_structure(outs, fx)
+    ref = ORACLES[key](*cpu_in)
+    ref = ref if isinstance(ref, (tuple, list)) else (ref,)
+    for i, (o, e, g) in enumerate(zip(outs, ref, fx["outputs"])):
+        oc = o.cpu()
+        rows = torch.tensor(g["rows"])
+        o2 = oc.reshape(-1, oc.shape[-1]) if oc.dim() > 1 else oc.reshape(1, -1)
+        if key in EXACT:
+            assert torch.equal(oc, e), "embedding gather must be bit exact"
+            assert torch.equal(o2[rows], g["values"]), "golden rows"
+        elif key in EMB_BWD:
+            ids = cpu_in[1]
+            f64 = F.embedding_bwd_f64(cpu_in[0], ids, 128256)
+            cnt = torch.bincount(ids.reshape(-1), minlength=128256).double()
+            assert_f32_close(oc, f64, "table gradient vs float64", atol=(1e-4 * cnt.sqrt()).unsqueeze(1))
+            untouched = cnt == 0
+            assert torch.count_nonzero(oc[untouched]) == 0
+        elif key in RMS_BWD and i == 1:
+            f64, _ = _dw_f64(key, cpu_in)
+            assert_bf16_close(oc.float(), e.float(), "dweight vs the reference graph", atol=5e-2)
+            if oc.dtype == torch.float32:
+                assert_f32_close(oc, f64, "dweight vs float64", atol=1e-3)
+        elif o.dtype == torch.float32:  # saved rstd
+            assert_f32_close(oc, e, f"output {i} (fp32)")
+            assert_f32_close(o2[rows], g["values"], f"output {i} golden rows")
+        else:
+            assert_bf16_close(oc, e, f"output {i}")
+            assert_bf16_close(o2[rows], g["values"], f"output {i} golden rows")

@@ -1,0 +1,173 @@
+"""Multi-rank host logic of kernelproblems_b200.sharding on CPU ranks (gloo,
+world size 2), with the CUDA kernels replaced by oracle functions: row
+sharding, the dweight exchange (all-gather + fixed-order sum, and plain
+all-reduce), the vocab-parallel embedding forward (masked gather +
+all-reduce) and backward (per-rank table-gradient shard), and host-side
+failure detection (a rank that raises before a collective)."""
+import datetime
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+WORLD = 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _entry(rank, fn, port, q, timeout_s):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=WORLD,
+                                timeout=datetime.timedelta(seconds=timeout_s))
+        res = fn(rank)
+        q.put((rank, "ok", res))
+    except Exception as e:  # reported to the parent, which asserts on it
+        q.put((rank, "error", f"{type(e).__name__}: {e}\n{traceback.format_exc()[-800:]}"))
+    finally:
+        if dist.is_initialized():
+            try:
+                dist.destroy_process_group()
+            except Exception:
+                pass
+
+
+def run_ranks(fn, timeout_s=30):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_entry, args=(r, fn, port, q, timeout_s)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(WORLD):
+        r, status, res = q.get(timeout=timeout_s * 4)
+        out[r] = (status, res)
+    for p in procs:
+        p.join(timeout=timeout_s)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+# ---- rank bodies (module level so spawn can pickle them) -------------------
+
+def _cpu_rms_bwd(dy, x, rstd, w, dy2=None, dres=None, eps=1e-6, dw_dtype=torch.float32):
+    from oracle import fragments as F
+    dxf, _ = F.add_rmsnorm_bwd(dy, dy2, x, rstd, w, dres)
+    g = dy if dy2 is None else torch.ops.aten.add.Tensor(dy, dy2)
+    return dxf, F.rmsnorm_dw_f64(g, x, rstd).float()
+
+
+def _ordered_sum(parts):
+    acc = torch.zeros(parts.shape[1], dtype=torch.float32)
+    for i in range(parts.shape[0]):
+        acc += parts[i]
+    return acc
+
+
+def _inputs(M=37, N=64):
+    from kernelproblems_b200 import configs as cf
+    from oracle import fragments as F
+    x = cf.randn((M, N), seed=1)
+    w = cf.rmsnorm_weight(N, seed=2)
+    dy = cf.randn((M, N), seed=3)
+    _, rstd = F.rmsnorm_fwd(x, w, 1e-6)
+    return x, w, dy, rstd.reshape(M)
+
+
+def _body_rms(rank, exact_order=True):
+    from kernelproblems_b200 import sharding
+    x, w, dy, rstd = _inputs()
+    rows = sharding.local_rows(x.shape[0])
+    sl = slice(rows.lo, rows.hi)
+    dx, dw = sharding.rmsnorm_bwd_dp(dy[sl].contiguous(), x[sl].contiguous(), rstd[sl].contiguous(), w,
+                                     exact_order=exact_order, bwd_fn=_cpu_rms_bwd,
+                                     reduce_fn=_ordered_sum)
+    return rows.lo, rows.hi, dx, dw
+
+
+def _body_rms_allreduce(rank):
+    return _body_rms(rank, exact_order=False)
+
+
+def _body_emb(rank):
+    from kernelproblems_b200 import configs as cf
+    from kernelproblems_b200 import sharding
+    from oracle import fragments as F
+    V, D = 50, 16
+    ids = torch.randint(0, V, (3, 11), generator=torch.Generator().manual_seed(5))
+    table = cf.randn((V, D), std=0.02, seed=6)
+    sh = sharding.vocab_shard(V)
+    out = sharding.embedding_fwd_vocab_parallel(
+        ids, table[sh.lo:sh.hi].contiguous(), sh.lo, V,
+        fwd_fn=lambda i, t, vocab_lo, vocab_total: F.embedding_fwd_vocab_shard(t, i, vocab_lo).float())
+    grad = cf.randn((3, 11, D), seed=7)
+    G = sharding.embedding_bwd_vocab_parallel(
+        grad, ids, sh.lo, sh.n, V,
+        bwd_fn=lambda g, i, n, vocab_lo, vocab_total, padding_idx: F.embedding_bwd_f64(
+            g, i, n, padding_idx, vocab_lo))
+    return sh.lo, sh.hi, out, G
+
+
+def _body_rank1_raises(rank):
+    t = torch.ones(4)
+    if rank == 1:
+        raise RuntimeError("rank 1 fails before the collective")
+    dist.all_reduce(t)  # rank 0 must get an error, not hang
+    return t
+
+
+# ---- tests ------------------------------------------------------------------
+
+@pytest.mark.parametrize("body", [_body_rms, _body_rms_allreduce])
+def test_rmsnorm_bwd_dp_two_ranks(body):
+    from oracle import fragments as F
+    out = run_ranks(body)
+    assert all(s == "ok" for s, _ in out.values()), out
+    x, w, dy, rstd = _inputs()
+    full_dx, _ = F.rmsnorm_bwd(dy, x, rstd, w)
+    full_dw = F.rmsnorm_dw_f64(dy, x, rstd)
+    dws = []
+    for r in range(WORLD):
+        lo, hi, dx, dw = out[r][1]
+        assert torch.equal(dx, full_dx[lo:hi]), "local rows only, unchanged"
+        assert torch.allclose(dw.double(), full_dw, rtol=1e-5, atol=1e-4)
+        dws.append(dw)
+    assert torch.equal(dws[0], dws[1]), "every rank holds the same dweight"
+
+
+def test_vocab_parallel_embedding_two_ranks():
+    from kernelproblems_b200 import configs as cf
+    from oracle import fragments as F
+    out = run_ranks(_body_emb)
+    assert all(s == "ok" for s, _ in out.values()), out
+    V, D = 50, 16
+    ids = torch.randint(0, V, (3, 11), generator=torch.Generator().manual_seed(5))
+    table = cf.randn((V, D), std=0.02, seed=6)
+    full = F.embedding_fwd(table, ids)
+    grad = cf.randn((3, 11, D), seed=7)
+    Gfull = F.embedding_bwd_f64(grad, ids, V)
+    covered = []
+    for r in range(WORLD):
+        lo, hi, o, G = out[r][1]
+        assert torch.equal(o.to(torch.bfloat16), full), "all-reduced gather is the exact row"
+        assert torch.equal(G, Gfull[lo:hi])
+        covered.append((lo, hi))
+    assert covered[0][0] == 0 and covered[-1][1] == V and covered[0][1] == covered[1][0]
+
+
+def test_rank_failure_is_reported_not_hung():
+    out = run_ranks(_body_rank1_raises, timeout_s=5)
+    assert out[1][0] == "error" and "fails before" in out[1][1]
+    assert out[0][0] == "error", "the surviving rank's collective must end with an error"
