@@ -51,7 +51,8 @@ enum frag_status {
   FRAG_ERR_ALIGN = 3,       /* misaligned pointer or stride                      */
   FRAG_ERR_WORKSPACE = 4,   /* workspace missing or smaller than the query says  */
   FRAG_ERR_CUDA = 5,        /* a CUDA runtime call or launch failed              */
-  FRAG_ERR_NO_DEVICE = 6    /* no CUDA device is visible                         */
+  FRAG_ERR_NO_DEVICE = 6,   /* no CUDA device is visible                         */
+  FRAG_ERR_SCRATCH_LIMIT = 7 /* needs more than the static scratch of a no-alloc entry point */
 };
 
 /* Bits written into a caller's device status word by kernels. */
@@ -131,6 +132,36 @@ FRAG_API int64_t frag_rmsnorm_bwd_num_blocks(int64_t M, int64_t N);
 /* Sum partials[G, N] over G in order into dw (fp32) and/or dw_bf16. */
 FRAG_API int frag_dw_reduce(const float* partials, int64_t G, int64_t N, float* dw,
                    void* dw_bf16, frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * RMSNorm backward that allocates nothing and takes no workspace.  This entry
+ * point has no counterpart in the reference (its Triton drop-ins allocate
+ * their scratch with torch.empty on every call).  It serves callers that
+ * cannot obtain device memory at call time: an executor that sizes all device
+ * memory before a training step and must not call cudaMalloc in the middle of
+ * it (cudaMalloc can synchronise the device and stall the queued work), or a
+ * plugin host whose ABI hands over tensors but neither an allocator nor a
+ * workspace argument.
+ * Arguments and results are those of frag_rmsnorm_bwd without the workspace.
+ * The scratch (per-block dweight partials; for the generic kernel also a copy
+ * of rstd) lives in one static device array of FRAG_NOALLOC_SCRATCH_BYTES
+ * (16 MiB) that every GPU loading this library holds until the process exits.
+ * A problem whose scratch would not fit returns FRAG_ERR_SCRATCH_LIMIT before
+ * anything is launched (the C1 and C4 configurations need about 4.9 MB).
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current).  Make that first call
+ *     before any stream capture.
+ *   - Every call uses the same array, which keeps the last call's contents.
+ *     Each call writes every scratch byte before reading it, so nothing has to
+ *     be cleared, but calls that overlap on the GPU (e.g. on two streams at
+ *     once) race on the array: keep such calls ordered on one stream.
+ *   - It calls no cudaMalloc, cudaFree or other allocating routine.
+ * ------------------------------------------------------------------------- */
+#define FRAG_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+FRAG_API int frag_rmsnorm_bwd_noalloc(const void* dy, const void* dy2, const void* x,
+                                      const float* rstd, const void* w, const void* dres,
+                                      void* dx_out, float* dw, void* dw_bf16, int64_t M,
+                                      int64_t N, float eps, frag_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Token-embedding gather (optionally one vocab shard of a vocab-parallel table).

@@ -21,6 +21,7 @@ STATUS_NAMES = {
     4: "FRAG_ERR_WORKSPACE",
     5: "FRAG_ERR_CUDA",
     6: "FRAG_ERR_NO_DEVICE",
+    7: "FRAG_ERR_SCRATCH_LIMIT",
 }
 FRAG_DEVFLAG_INDEX_OOB = 1
 FRAG_ROPE_NEOX = 0
@@ -72,6 +73,8 @@ SIGNATURES: dict[str, tuple] = {
         _int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp, _sz, _vp],
     ),
+    "frag_rmsnorm_bwd_noalloc": (
+        _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     "frag_rmsnorm_bwd_num_blocks": (_i64, [_i64, _i64]),
     "frag_dw_reduce": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "frag_embedding_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),

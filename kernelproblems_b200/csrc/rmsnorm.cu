@@ -18,6 +18,7 @@
 // instruction of a block is one fully coalesced span — and each element is
 // read from HBM exactly once.  Generic path: any N, two passes over the row.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -568,3 +569,59 @@ int frag_rmsnorm_bwd(const void* dy, const void* dy2, const void* x, const float
 }
 
 }  // extern "C"
+
+// ----------------------------------------------- backward without a workspace
+//
+// frag_rmsnorm_bwd_noalloc runs frag_rmsnorm_bwd with a file-scope device
+// array as its workspace, for callers that cannot allocate (see frag.h).
+
+namespace frag {
+namespace {
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[FRAG_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// In host code `g_noalloc_scratch` names a host-side shadow, not device
+// memory; the device address is looked up once per device, with that device
+// current, and cached.
+int noalloc_scratch_address(void** out) {
+  const int d = current_device();
+  if (d < 0 || d >= 64) return FRAG_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_addr[d] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      set_last_cuda_error(e);
+      return FRAG_ERR_CUDA;
+    }
+    g_noalloc_addr[d] = p;
+  }
+  *out = g_noalloc_addr[d];
+  return FRAG_OK;
+}
+
+}  // namespace
+}  // namespace frag
+
+extern "C" int frag_rmsnorm_bwd_noalloc(const void* dy, const void* dy2, const void* x,
+                                        const float* rstd, const void* w, const void* dres,
+                                        void* dx_out, float* dw, void* dw_bf16, int64_t M,
+                                        int64_t N, float eps, frag_stream_t stream) {
+  if (M < 0 || N < 0) return FRAG_ERR_INVALID_ARG;
+  if (M == 0 || N == 0)  // nothing to reduce: no scratch needed
+    return frag_rmsnorm_bwd(dy, dy2, x, rstd, w, dres, dx_out, dw, dw_bf16, M, N, eps, nullptr,
+                            0, stream);
+  bool aligned = aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx_out) &&
+                 aligned16(dy2) && aligned16(dres);
+  const BwdPlan pl = make_bwd_plan(M, N, aligned);
+  if (bwd_workspace_bytes(pl, M, N) > FRAG_NOALLOC_SCRATCH_BYTES) return FRAG_ERR_SCRATCH_LIMIT;
+  void* ws = nullptr;
+  const int st = noalloc_scratch_address(&ws);
+  if (st != FRAG_OK) return st;
+  return frag_rmsnorm_bwd(dy, dy2, x, rstd, w, dres, dx_out, dw, dw_bf16, M, N, eps, ws,
+                          FRAG_NOALLOC_SCRATCH_BYTES, stream);
+}

@@ -51,6 +51,8 @@ const char* frag_status_string(int status) {
     case FRAG_ERR_WORKSPACE: return "workspace missing or too small";
     case FRAG_ERR_CUDA: return "CUDA runtime error";
     case FRAG_ERR_NO_DEVICE: return "no CUDA device";
+    case FRAG_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the no-alloc entry point's static buffer holds";
     default: return "unknown status";
   }
 }

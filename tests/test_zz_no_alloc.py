@@ -1,0 +1,89 @@
+"""frag_rmsnorm_bwd_noalloc: the RMSNorm backward for callers that cannot
+allocate device memory when they call it (an executor that sizes all memory
+before a step and must not cudaMalloc mid-step, or a plugin host that passes
+tensors but no allocator or workspace).  Its scratch is a static 16 MiB device
+array inside libfrag.so.
+
+Checked through the C ABI against frag_rmsnorm_bwd (which takes a caller
+workspace) on two calls in a row, within the parity tolerances of the other
+tests.  This file is collected last on purpose: a first-failure run has
+already run every other test by the time it gets here; it must also pass on
+its own in a fresh process."""
+import ctypes as C
+
+import pytest
+import torch
+
+from conftest import assert_bf16_close, assert_f32_close
+from kernelproblems_b200 import _lib
+from kernelproblems_b200 import configs as cf
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _p(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _case(shape, variant, seed):
+    N = shape[-1]
+    x = cf.randn(shape, device=DEV, seed=seed)
+    w = cf.rmsnorm_weight(N, device=DEV, seed=seed + 1)
+    dy = cf.randn(shape, device=DEV, seed=seed + 2)
+    xf = x.float()
+    rstd = torch.rsqrt(xf.pow(2).mean(-1) + 1e-6).contiguous()
+    dy2 = cf.randn(shape, device=DEV, seed=seed + 3) if variant == "add_add" else None
+    dres = cf.randn(shape, device=DEV, seed=seed + 4) if variant == "add_add" else None
+    r = None if variant == "recompute" else rstd
+    return x, w, dy, r, dy2, dres
+
+
+def _with_workspace(lib, x, w, dy, r, dy2, dres):
+    N = w.numel()
+    M = x.numel() // N
+    dx = torch.empty_like(x)
+    dw = torch.empty(N, dtype=torch.float32, device=DEV)
+    ws = torch.empty(max(16, lib.frag_rmsnorm_bwd_workspace_bytes(M, N)), dtype=torch.uint8, device=DEV)
+    st = lib.frag_rmsnorm_bwd(_p(dy), _p(dy2), _p(x), _p(r), _p(w), _p(dres), _p(dx), _p(dw), None,
+                              M, N, 1e-6, _p(ws), ws.numel(), _stream())
+    assert st == 0, lib.frag_status_string(st)
+    return dx, dw
+
+
+def _no_alloc(lib, x, w, dy, r, dy2, dres):
+    N = w.numel()
+    M = x.numel() // N
+    dx = torch.empty_like(x)
+    dw = torch.empty(N, dtype=torch.float32, device=DEV)
+    st = lib.frag_rmsnorm_bwd_noalloc(_p(dy), _p(dy2), _p(x), _p(r), _p(w), _p(dres), _p(dx), _p(dw),
+                                      None, M, N, 1e-6, _stream())
+    assert st == 0, lib.frag_status_string(st)
+    return dx, dw
+
+
+@pytest.mark.parametrize("shape,variant", [((4, 2048, 4096), "saved_rstd"),   # C1
+                                           ((2, 4096, 8192), "add_add"),      # C4 width, fused adds
+                                           ((37, 1000), "recompute")])        # generic kernels
+def test_no_alloc_matches_workspace_entry_point(shape, variant):
+    lib = _lib.load()
+    args = _case(shape, variant, seed=len(shape) * 100 + shape[-1])
+    ref_dx, ref_dw = _with_workspace(lib, *args)
+    for _ in range(2):  # the static scratch keeps the previous call's contents
+        dx, dw = _no_alloc(lib, *args)
+        torch.cuda.synchronize()
+        assert_bf16_close(dx, ref_dx, "dx")
+        assert_f32_close(dw, ref_dw, "dweight", atol=1e-4)
+
+
+def test_no_alloc_rejects_problems_beyond_its_scratch():
+    lib = _lib.load()
+    # generic kernel (N % 8 != 0) keeps a copy of rstd: 5M rows need 20 MB > 16 MiB
+    st = lib.frag_rmsnorm_bwd_noalloc(None, None, None, None, None, None, None, None, None,
+                                      5_000_000, 1000, 1e-6, _stream())
+    assert st == 7
+    assert b"static buffer" in lib.frag_status_string(st)
