@@ -183,36 +183,83 @@ class Frag:
     """One fragment at its configuration on this rank: device-resident inputs,
     preallocated outputs, and the list of launch stages."""
 
-    def __init__(self, name, desc, tokens, nbytes, stages, exchange=None, e2e=None,
-                 kernels=None):
+    def __init__(self, name, desc, tokens, nbytes, stages, exchange=None, e2e=None):
         self.name, self.desc, self.tokens, self.bytes = name, desc, tokens, nbytes
         self.stages = stages          # [(label, callable)] local launches
-        self.exchange = exchange      # callable or None (NCCL, eager)
-        self.e2e = e2e                # callable(host_inputs) -> (h2d, d2h) via the public API
-        self.kernels = kernels or {}
-        self.graphs = []
+        self.exchange = exchange      # callable or None (NCCL, run eagerly)
+        self.e2e = e2e                # callable(host buffers) -> (h2d, d2h) via the public API
         self.kernel_nodes = 0
+        self.ev = []                  # timing events: start, after each stage
+        self.ev_end = None            # after the exchange (eager)
 
-    def capture(self, use_graphs: bool):
-        for _, fn in self.stages:  # warm: load modules, size workspaces
-            fn()
-        torch.cuda.synchronize()
-        self.graphs = []
-        if not use_graphs:
-            return
-        for label, fn in self.stages:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+
+class Step:
+    """The suite step.  Fragments are captured into CUDA graphs, one graph per
+    run of fragments between NCCL exchanges (the whole step at N=1), with
+    timing events recorded inside the graphs (external event nodes)."""
+
+    def __init__(self, frags, use_graphs: bool):
+        self.frags = frags
+        for f in frags:  # warm: load kernels, size workspaces, first launches
+            for _, fn in f.stages:
                 fn()
-            self.graphs.append(g)
-            self.kernel_nodes += max(count_kernel_nodes(g), 0)
         torch.cuda.synchronize()
+        segs, cur = [], []
+        for f in frags:
+            cur.append(f)
+            if f.exchange is not None:
+                segs.append(cur)
+                cur = []
+        if cur:
+            segs.append(cur)
+        self.segments = []
+        self.use_graphs = use_graphs
+        for seg in segs:
+            for f in seg:
+                f.ev = [torch.cuda.Event(enable_timing=True, external=use_graphs)
+                        for _ in range(len(f.stages) + 1)]
+                f.ev_end = torch.cuda.Event(enable_timing=True) if f.exchange is not None else None
+            g = None
+            if use_graphs:
+                g = torch.cuda.CUDAGraph(keep_graph=True)
+                with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                    self._launch(seg)
+                n = count_kernel_nodes(g)
+                for f in seg:
+                    f.kernel_nodes = 0
+                seg[0].kernel_nodes = max(n, 0)  # per segment; summed below
+                g.instantiate()
+            self.segments.append((g, seg))
+        torch.cuda.synchronize()
+        self.kernel_nodes = sum(f.kernel_nodes for f in frags) if use_graphs else None
 
-    def launch_stage(self, i):
-        if self.graphs:
-            self.graphs[i].replay()
-        else:
-            self.stages[i][1]()
+    @staticmethod
+    def _launch(seg):
+        for f in seg:
+            f.ev[0].record()
+            for si, (_, fn) in enumerate(f.stages):
+                fn()
+                f.ev[si + 1].record()
+
+    def run(self):
+        for g, seg in self.segments:
+            if g is not None:
+                g.replay()
+            else:
+                self._launch(seg)
+            last = seg[-1]
+            if last.exchange is not None:
+                last.exchange()
+                last.ev_end.record()
+
+    def breakdown(self):
+        """Per-fragment and per-stage ms of the last completed step."""
+        out = {}
+        for f in self.frags:
+            st = [f.ev[i].elapsed_time(f.ev[i + 1]) for i in range(len(f.stages))]
+            end = f.ev_end if f.ev_end is not None else f.ev[-1]
+            out[f.name] = (f.ev[0].elapsed_time(end), st)
+        return out
 
 
 def scaled_configs(frac: float):
@@ -521,30 +568,14 @@ def ours_arm(args, rank, local_rank, world):
         return emb_vp_arm(args, rank, world, dev, pg)
     names = SUITE if args.workload == "suite" else [args.workload]
     frags = build_suite(dev, world, rank, names, pg, args.rows_frac)
-    for f in frags:
-        f.capture(not args.no_graphs)
+    step = Step(frags, not args.no_graphs)
     step_bytes = sum(f.bytes for f in frags)
     stream = torch.cuda.current_stream(dev)
 
-    def one_step(evs=None):
-        for fi, f in enumerate(frags):
-            if evs is not None:
-                evs[fi][0].record(stream)
-            for si in range(len(f.stages)):
-                f.launch_stage(si)
-                if evs is not None:
-                    evs[fi][1 + si].record(stream)
-            if f.exchange is not None:
-                f.exchange()
-            if evs is not None:
-                evs[fi][-1].record(stream)
-
     for _ in range(max(3, args.warmup)):
-        one_step()
+        step.run()
     torch.cuda.synchronize()
     K = args.steps
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(len(f.stages) + 2)] for f in frags]
-           for _ in range(K)]
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local_rank, enabled=(rank == 0 and not args.no_clocks))
@@ -552,24 +583,26 @@ def ours_arm(args, rank, local_rank, world):
         dist.barrier()
     torch.cuda.synchronize()
     t_start.record(stream)
-    for k in range(K):
-        one_step(evs[k])
+    for _ in range(K):
+        step.run()
     t_end.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
     total_ms = t_start.elapsed_time(t_end)
+    # per-fragment / per-stage breakdown: the same step replayed R more times,
+    # read from the events inside the step after each replay
+    R = max(5, min(K, 30))
     frag_ms = {f.name: [] for f in frags}
     stage_ms = {f.name: [[] for _ in f.stages] for f in frags}
-    for k in range(K):
-        for fi, f in enumerate(frags):
-            e = evs[k][fi]
-            frag_ms[f.name].append(e[0].elapsed_time(e[-1]))
-            prev = e[0]
-            for si in range(len(f.stages)):
-                stage_ms[f.name][si].append(prev.elapsed_time(e[1 + si]))
-                prev = e[1 + si]
+    for _ in range(R):
+        step.run()
+        torch.cuda.synchronize()
+        for name, (fm, st) in step.breakdown().items():
+            frag_ms[name].append(fm)
+            for i, v in enumerate(st):
+                stage_ms[name][i].append(v)
     # max over ranks
     tmax = torch.tensor([total_ms] + [statistics.fmean(frag_ms[f.name]) for f in frags],
                         dtype=torch.float64, device=dev)
@@ -588,7 +621,7 @@ def ours_arm(args, rank, local_rank, world):
                       "pct_of_8TBs": round(100 * f.bytes / (ms * 1e-3) / 1e9 / NOMINAL_HBM_GBS, 1),
                       "frac_of_measured": round(f.bytes / (ms * 1e-3) / 1e9 / peak, 3),
                       "tokens_per_s": round(world * f.tokens / (ms * 1e-3)),
-                      "bytes": f.bytes, "tokens": f.tokens, "kernels": f.kernel_nodes,
+                      "bytes": f.bytes, "tokens": f.tokens,
                       "stages_ms": {lab: round(statistics.fmean(stage_ms[f.name][si]), 4)
                                     for si, (lab, _) in enumerate(f.stages)}}
     roof = None
@@ -605,7 +638,9 @@ def ours_arm(args, rank, local_rank, world):
             "algorithmic_bytes_per_launch": dom.bytes, "launch_ms": round(main_ms, 4),
             "peak_source": peak_note, "pct_of_8TBs": round(100 * achieved / NOMINAL_HBM_GBS, 1)}
 
-    launches = sum(f.kernel_nodes for f in frags) * K if not args.no_graphs else None
+    # graph kernel nodes (ours and the sort's) + the eager dw_reduce of each exchange
+    n_ex = sum(1 for f in frags if f.exchange is not None)
+    launches = (step.kernel_nodes + n_ex) * K if step.kernel_nodes is not None else None
     line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -623,8 +658,7 @@ def ours_arm(args, rank, local_rank, world):
         line["e2e"] = e2e_measure(frags, args.e2e_steps, world, dev, step_bytes)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(names, args.cpu_seconds)
-    for f in frags:
-        f.graphs = []
+    step.segments = []
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -57,7 +57,8 @@ enum frag_status {
 
 /* Bits written into a caller's device status word by kernels. */
 enum frag_devflag {
-  FRAG_DEVFLAG_INDEX_OOB = 1 /* an embedding id was outside [0, vocab_total)     */
+  FRAG_DEVFLAG_INDEX_OOB = 1,   /* an embedding id was outside [0, vocab_total)  */
+  FRAG_DEVFLAG_WAIT_TIMEOUT = 2 /* a kernel gave up waiting for its own copies  */
 };
 
 /* RoPE layouts.  NEOX pairs element i with i + D/2 (rotate-half);
@@ -235,6 +236,12 @@ FRAG_API int frag_rope(const frag_rope_tensor* tensors, int num_tensors, int64_t
 
 /* Device properties the host layer uses to size launches and workspaces. */
 FRAG_API int frag_device_sm_count(void);
+
+/* Error bits (FRAG_DEVFLAG_*) that kernels on the current device recorded in
+ * the library's own error word (a static device variable), e.g. a bounded
+ * wait that expired.  Synchronises the device to read it; clears it if
+ * `clear` is non-zero.  Returns the bits (>= 0) or -FRAG_ERR_CUDA. */
+FRAG_API int frag_device_errors(int clear);
 
 #ifdef __cplusplus
 }

@@ -24,6 +24,7 @@ STATUS_NAMES = {
     7: "FRAG_ERR_SCRATCH_LIMIT",
 }
 FRAG_DEVFLAG_INDEX_OOB = 1
+FRAG_DEVFLAG_WAIT_TIMEOUT = 2
 FRAG_ROPE_NEOX = 0
 FRAG_ROPE_INTERLEAVED = 1
 FRAG_POS_NONE = 0
@@ -66,6 +67,7 @@ SIGNATURES: dict[str, tuple] = {
     "frag_status_string": (C.c_char_p, [_int]),
     "frag_last_cuda_error": (_int, []),
     "frag_device_sm_count": (_int, []),
+    "frag_device_errors": (_int, [_int]),
     "frag_rmsnorm_fwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     "frag_add_rmsnorm_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     "frag_rmsnorm_bwd_workspace_bytes": (_sz, [_i64, _i64]),

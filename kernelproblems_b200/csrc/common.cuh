@@ -42,6 +42,11 @@ inline bool aligned16(const void* p) {
 
 // Number of SMs on the current device (cached per device).
 int sm_count();
+// Device address of the library's error word on the current device (kernels
+// atomicOr FRAG_DEVFLAG_* bits into it), or nullptr if it cannot be found.
+int* device_error_word();
+// Opt a kernel into `bytes` of dynamic shared memory (once per kernel/device).
+bool allow_dynamic_smem(const void* kernel, int bytes);
 // Current device ordinal or -1.
 int current_device();
 
@@ -163,6 +168,61 @@ __device__ __forceinline__ float block_sum(float v, float (*slots)[32], int pari
   float t = 0.f;
   for (int i = 0; i < nw; ++i) t += slots[parity][i];
   return t;
+}
+
+// --------------------------------------------- TMA bulk copies + mbarriers
+//
+// One-dimensional bulk copies (cp.async.bulk) move whole rows from global to
+// shared memory asynchronously; an mbarrier per stage counts the bytes in.
+// Every wait is bounded: after kWaitCycles it sets FRAG_DEVFLAG_WAIT_TIMEOUT
+// in the error word and returns false instead of spinning forever.
+
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for phase `parity` of `bar` to complete; false (and the error bit set)
+// if it has not after kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      if (err) atomicOr(err, FRAG_DEVFLAG_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+// Global -> shared bulk copy of `bytes` (multiple of 16, both addresses
+// 16-byte aligned), completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 }  // namespace frag

@@ -12,12 +12,13 @@
 //             last for padding / out-of-shard ids), val[t] = t
 //   2. sort:  stable LSD radix sort of (key, val) — tokens of one row end up
 //             contiguous and in increasing t order
-//   3. rows:  every table row of the shard is owned by exactly one CTA, which
-//             sums that row's token gradients in t order in fp32 registers and
-//             writes the row once (zero rows included: no separate memset of
-//             the 2 GB gradient).  Summation order is fixed by (ids, t), so the
-//             result is bitwise reproducible, unlike the fp32-atomic reference
-//             kernel (v7/a12a160cb11b/optimized_kernel.py:34).
+//   3. rows:  every table row of the shard is written exactly once (no
+//             separate memset of the 2 GB gradient): rows without tokens as
+//             zeros, rows with tokens as the fp32 sum of their gradient rows in
+//             increasing t (emb_bwd_zero + emb_bwd_tokens).  Summation order is
+//             fixed by (ids, t), so the result is bitwise reproducible, unlike
+//             the fp32-atomic reference kernel
+//             (v7/a12a160cb11b/optimized_kernel.py:34).
 #include <cub/device/device_radix_sort.cuh>
 
 #include <algorithm>
@@ -76,10 +77,12 @@ emb_fwd_generic(const int64_t* __restrict__ ids, const uint16_t* __restrict__ ta
 
 // ----------------------------------------------------------------- backward
 
+// keys/values for the sort, plus a bitmap of the shard rows that have tokens
+// (zeroed by the caller).
 __global__ void __launch_bounds__(256)
 emb_bwd_prep(const int64_t* __restrict__ ids, int T, int64_t vocab_lo, int64_t shard_rows,
              int64_t vocab_total, int64_t padding_idx, uint32_t* __restrict__ keys,
-             uint32_t* __restrict__ vals, int32_t* status) {
+             uint32_t* __restrict__ vals, uint32_t* __restrict__ touched, int32_t* status) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   const int64_t id = ids[t];
@@ -89,6 +92,7 @@ emb_bwd_prep(const int64_t* __restrict__ ids, int T, int64_t vocab_lo, int64_t s
   const bool ok = !oob && id != padding_idx && v >= 0 && v < shard_rows;
   keys[t] = ok ? static_cast<uint32_t>(v) : static_cast<uint32_t>(shard_rows);
   vals[t] = static_cast<uint32_t>(t);
+  if (ok && touched) atomicOr(&touched[v >> 5], 1u << (v & 31));
 }
 
 // First index i in [0, n) with keys[i] >= target (n if none), keys sorted
@@ -111,9 +115,11 @@ __device__ int warp_lower_bound(const uint32_t* __restrict__ keys, int n, uint32
   return lo + __popc(__ballot_sync(0xffffffffu, less));
 }
 
-// Rows [b*R, min(shard_rows, (b+1)*R)) belong to CTA b.  Thread i owns
-// 16-byte column chunks i, i+256, ... (KPT of them), so each row is summed in
-// registers and written with 128-bit streaming stores.
+// Rows [b*R, min(shard_rows, (b+1)*R)) belong to CTA b.  Thread i owns the
+// 4-column groups i, i+256, ... (KPT of them): it reads 8-byte bf16 quads and
+// writes 16-byte fp32 quads, so every load and store instruction of a warp is
+// one contiguous span (a thread owning 8 columns would write two float4s 32 B
+// apart per instruction and half-fill every sector: ~45% slower on B200).
 template <int KPT>
 __global__ void __launch_bounds__(256)
 emb_bwd_rows_vec(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, int T,
@@ -131,14 +137,12 @@ emb_bwd_rows_vec(const uint32_t* __restrict__ keys, const uint32_t* __restrict__
   __syncthreads();
   int p = bounds[0];
   const int pend = bounds[1];
-  const int chunks = D >> 3;
+  const int quads = D >> 2;
 
   for (int64_t v = lo; v < hi; ++v) {
-    float acc[KPT][8];
+    float4 acc[KPT];
 #pragma unroll
-    for (int k = 0; k < KPT; ++k)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
+    for (int k = 0; k < KPT; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     // Tokens of row v: keys[p..] == v (uniform across the CTA).
     while (p < pend && keys[p] == static_cast<uint32_t>(v)) {
       // Up to 4 tokens of the run per round: their loads are all issued
@@ -151,16 +155,20 @@ emb_bwd_rows_vec(const uint32_t* __restrict__ keys, const uint32_t* __restrict__
         tok[j] = has[j] ? static_cast<int>(vals[p]) : 0;
         if (has[j]) ++p;
       }
-      uint4 gv[4][KPT];
+      uint2 gv[4][KPT];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (has[j]) {
+          const uint16_t* src = grad + static_cast<int64_t>(tok[j]) * D;
 #pragma unroll
           for (int k = 0; k < KPT; ++k) {
-            const int c = threadIdx.x + k * 256;
-            gv[j][k] = (c < chunks)
-                           ? ld_stream(grad + static_cast<int64_t>(tok[j]) * D + c * 8)
-                           : make_uint4(0, 0, 0, 0);
+            const int q = threadIdx.x + k * 256;
+            if (q < quads) {
+              asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                           : "=r"(gv[j][k].x), "=r"(gv[j][k].y) : "l"(src + q * 4));
+            } else {
+              gv[j][k] = make_uint2(0, 0);
+            }
           }
         }
       }
@@ -170,22 +178,111 @@ emb_bwd_rows_vec(const uint32_t* __restrict__ keys, const uint32_t* __restrict__
         if (has[j]) {
 #pragma unroll
           for (int k = 0; k < KPT; ++k) {
-            float f[8];
-            unpack8(gv[j][k], f);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[k][i] += f[i];
+            acc[k].x += bf16lo(gv[j][k].x);
+            acc[k].y += bf16hi(gv[j][k].x);
+            acc[k].z += bf16lo(gv[j][k].y);
+            acc[k].w += bf16hi(gv[j][k].y);
           }
         }
       }
     }
-    float* row = G + v * static_cast<int64_t>(D);
+    float4* row = reinterpret_cast<float4*>(G + v * static_cast<int64_t>(D));
 #pragma unroll
     for (int k = 0; k < KPT; ++k) {
-      const int c = threadIdx.x + k * 256;
-      if (c < chunks) {
-        st_stream_f4(row + c * 8, make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]));
-        st_stream_f4(row + c * 8 + 4, make_float4(acc[k][4], acc[k][5], acc[k][6], acc[k][7]));
+      const int q = threadIdx.x + k * 256;
+      if (q < quads) st_stream_f4(row + q, acc[k]);
+    }
+  }
+}
+
+// Default row kernels (widths that are multiples of 8, up to 4096), two
+// launches that together write every table row of the shard exactly once:
+//
+// emb_bwd_zero: every row the bitmap does not mark is zeroed by a grid-stride
+//   sweep in 32-byte units with 256-bit stores.  All CTAs write neighbouring
+//   addresses at the same time, which on B200 streams at ~6.9 TB/s (a CTA per
+//   block of rows reaches ~6.2 TB/s).
+// emb_bwd_tokens: many small CTAs, each owning the runs (rows) that start in
+//   its slice of kTokPerCta sorted tokens; a run's gradient rows are added in
+//   token order in fp32 and the row is written once.  Thousands of CTAs keep
+//   enough runs in flight to hide each run's dependent load chain.
+constexpr int kTokPerCta = 8;
+
+__global__ void __launch_bounds__(256)
+emb_bwd_zero(const uint32_t* __restrict__ touched, float* __restrict__ G, int64_t shard_rows, int D) {
+  const int units_row = D >> 3;
+  const int64_t total = shard_rows * units_row;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < total;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = u / units_row;
+    if (__ldg(touched + (row >> 5)) & (1u << (row & 31))) continue;
+    asm volatile("st.global.cs.v8.f32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"l"(G + u * 8), "f"(0.f)
+                 : "memory");
+  }
+}
+
+template <int U>  // 8-float units per thread and row (128 threads)
+__global__ void __launch_bounds__(128)
+emb_bwd_tokens(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, int T,
+               const uint16_t* __restrict__ grad, float* __restrict__ G, int64_t shard_rows, int D) {
+  __shared__ int bounds[2];
+  const int warp = threadIdx.x >> 5;
+  if (warp < 2) {
+    // slice start/end moved forward to the first run that starts at or after it
+    int sx = static_cast<int>(min(static_cast<int64_t>(T),
+                                  (static_cast<int64_t>(blockIdx.x) + warp) * kTokPerCta));
+    if (sx > 0 && sx < T && __ldg(keys + sx) == __ldg(keys + sx - 1))
+      sx = warp_lower_bound(keys, T, __ldg(keys + sx - 1) + 1);
+    if ((threadIdx.x & 31) == 0) bounds[warp] = sx;
+  }
+  __syncthreads();
+  int q = bounds[0];
+  const int s1 = bounds[1];
+  const int units_row = D >> 3;
+  while (q < s1) {
+    const uint32_t key = __ldg(keys + q);
+    if (key >= static_cast<uint64_t>(shard_rows)) break;  // padding / other shards sort last
+    float acc[U][8];
+#pragma unroll
+    for (int k = 0; k < U; ++k)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[k][e] = 0.f;
+    while (q < s1 && __ldg(keys + q) == key) {
+      // two tokens per round: both loads in flight, then the in-order adds
+      const bool two = q + 1 < s1 && __ldg(keys + q + 1) == key;
+      const uint16_t* s0p = grad + static_cast<int64_t>(__ldg(vals + q)) * D;
+      const uint16_t* s1p = two ? grad + static_cast<int64_t>(__ldg(vals + q + 1)) * D : s0p;
+      uint4 g0[U], g1[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const int c = threadIdx.x + k * 128;
+        const bool in = c < units_row;
+        g0[k] = in ? ld_stream(s0p + c * 8) : make_uint4(0, 0, 0, 0);
+        g1[k] = (in && two) ? ld_stream(s1p + c * 8) : make_uint4(0, 0, 0, 0);
       }
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        float f[8];
+        unpack8(g0[k], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[k][e] += f[e];
+        if (two) {
+          unpack8(g1[k], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[k][e] += f[e];
+        }
+      }
+      q += two ? 2 : 1;
+    }
+    float* row = G + static_cast<int64_t>(key) * D;
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const int c = threadIdx.x + k * 128;
+      if (c < units_row)
+        asm volatile("st.global.cs.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(row + c * 8),
+                     "f"(acc[k][0]), "f"(acc[k][1]), "f"(acc[k][2]), "f"(acc[k][3]), "f"(acc[k][4]),
+                     "f"(acc[k][5]), "f"(acc[k][6]), "f"(acc[k][7])
+                     : "memory");
     }
   }
 }
@@ -218,7 +315,7 @@ emb_bwd_rows_generic(const uint32_t* __restrict__ keys, const uint32_t* __restri
 }
 
 struct BwdLayout {
-  size_t keys_in, vals_in, keys_out, vals_out, temp, temp_bytes, total;
+  size_t keys_in, vals_in, keys_out, vals_out, touched, touched_bytes, temp, temp_bytes, total;
 };
 
 int sort_end_bit(int64_t shard_rows) {
@@ -243,7 +340,9 @@ bool bwd_layout(int64_t T, int64_t shard_rows, BwdLayout* L) {
   L->vals_in = a;
   L->keys_out = 2 * a;
   L->vals_out = 3 * a;
-  L->temp = 4 * a;
+  L->touched = 4 * a;
+  L->touched_bytes = align_up(static_cast<size_t>((shard_rows + 31) / 32) * 4, 256);
+  L->temp = L->touched + L->touched_bytes;
   L->temp_bytes = align_up(temp_bytes, 256);
   L->total = L->temp + L->temp_bytes;
   return true;
@@ -307,11 +406,13 @@ int frag_embedding_bwd(const int64_t* ids, const void* grad, float* G, int64_t T
   auto vals_in = reinterpret_cast<uint32_t*>(ws + L.vals_in);
   auto keys_out = reinterpret_cast<uint32_t*>(ws + L.keys_out);
   auto vals_out = reinterpret_cast<uint32_t*>(ws + L.vals_out);
+  auto touched = reinterpret_cast<uint32_t*>(ws + L.touched);
   const int Ti = static_cast<int>(T);
 
+  if (cuda_status(cudaMemsetAsync(touched, 0, L.touched_bytes, s)) != FRAG_OK) return FRAG_ERR_CUDA;
   if (Ti > 0) {
     emb_bwd_prep<<<dim3(static_cast<unsigned>(ceil_div(T, 256))), 256, 0, s>>>(
-        ids, Ti, vocab_lo, shard_rows, vocab_total, padding_idx, keys_in, vals_in, status);
+        ids, Ti, vocab_lo, shard_rows, vocab_total, padding_idx, keys_in, vals_in, touched, status);
     int st = check_launch();
     if (st != FRAG_OK) return st;
     size_t tb = L.temp_bytes;
@@ -321,21 +422,55 @@ int frag_embedding_bwd(const int64_t* ids, const void* grad, float* G, int64_t T
       return FRAG_ERR_CUDA;
   }
 
+  auto g = static_cast<const uint16_t*>(grad);
+  const int64_t quads = D / 4;
+  const bool vec = D % 4 == 0 && quads <= 8 * 256 && (Ti == 0 || (reinterpret_cast<uintptr_t>(grad) & 7) == 0) &&
+                   aligned16(G);
+  // One wave of CTAs, each owning a contiguous block of rows.
+  int per_sm = 0;
+  cudaError_t oe;
+  if (!vec) oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, emb_bwd_rows_generic, 256, 0);
+  else if (quads <= 256) oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, emb_bwd_rows_vec<1>, 256, 0);
+  else if (quads <= 512) oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, emb_bwd_rows_vec<2>, 256, 0);
+  else if (quads <= 1024) oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, emb_bwd_rows_vec<4>, 256, 0);
+  else oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, emb_bwd_rows_vec<8>, 256, 0);
+  if (oe != cudaSuccess) {
+    cudaGetLastError();
+    per_sm = 4;
+  }
   int sms = sm_count();
   if (sms <= 0) sms = 148;
-  const int64_t target = std::max<int64_t>(1, std::min<int64_t>(shard_rows, static_cast<int64_t>(sms) * 8));
+  const int64_t target =
+      std::max<int64_t>(1, std::min<int64_t>(shard_rows, static_cast<int64_t>(sms) * std::max(per_sm, 1)));
   const int64_t rpb = ceil_div(shard_rows, target);
   const dim3 grid(static_cast<unsigned>(ceil_div(shard_rows, rpb)));
-  auto g = static_cast<const uint16_t*>(grad);
-  const int64_t chunks = D / 8;
-  const bool vec = D % 8 == 0 && chunks <= 8 * 256 && (Ti == 0 || aligned16(grad)) && aligned16(G);
+  // Zero sweep + token CTAs: widths that are multiples of 8 up to 4096, rows
+  // 32-byte aligned (256-bit stores) and gradient rows 16-byte aligned.
+  const int64_t units = D / 8;
+  if (D % 8 == 0 && units <= 4 * 128 && (reinterpret_cast<uintptr_t>(G) & 31) == 0 &&
+      (Ti == 0 || aligned16(grad))) {
+    const int Di = static_cast<int>(D);
+    const int64_t zgrid = std::min<int64_t>(static_cast<int64_t>(sms) * 32,
+                                            std::max<int64_t>(1, ceil_div(shard_rows * units, 256)));
+    emb_bwd_zero<<<dim3(static_cast<unsigned>(zgrid)), 256, 0, s>>>(touched, G, shard_rows, Di);
+    int st2 = check_launch();
+    if (st2 != FRAG_OK || Ti == 0) return st2;
+    const dim3 tgrid(static_cast<unsigned>(ceil_div(T, kTokPerCta)));
+    if (units <= 128)
+      emb_bwd_tokens<1><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
+    else if (units <= 256)
+      emb_bwd_tokens<2><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
+    else
+      emb_bwd_tokens<4><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
+    return check_launch();
+  }
   if (vec) {
     const int Di = static_cast<int>(D);
-    if (chunks <= 256)
+    if (quads <= 256)
       emb_bwd_rows_vec<1><<<grid, 256, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di, rpb);
-    else if (chunks <= 512)
+    else if (quads <= 512)
       emb_bwd_rows_vec<2><<<grid, 256, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di, rpb);
-    else if (chunks <= 1024)
+    else if (quads <= 1024)
       emb_bwd_rows_vec<4><<<grid, 256, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di, rpb);
     else
       emb_bwd_rows_vec<8><<<grid, 256, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di, rpb);

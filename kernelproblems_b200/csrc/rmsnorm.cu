@@ -300,14 +300,160 @@ rmsnorm_bwd_vec(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block) {
     cr = nr;
   }
 
-  float* part = p.partials + static_cast<size_t>(blockIdx.x) * N;
+  // Write this block's partials [N] with contiguous 16-byte stores: a warp's
+  // 32 chunks (8 floats each) become 64 float4s; lane l stores float4
+  // 2*base + l (and + 32), taken from lane l/2 (16 + l/2) by shuffles.
+  float4* part = reinterpret_cast<float4*>(p.partials + static_cast<size_t>(blockIdx.x) * N);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int base = (threadIdx.x & ~31) + k * blockDim.x;  // chunk of lane 0
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int src = half * 16 + (lane >> 1);
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __shfl_sync(0xffffffffu, acc[k][i], src);
+      const bool hi = lane & 1;
+      const float4 o = hi ? make_float4(v[4], v[5], v[6], v[7]) : make_float4(v[0], v[1], v[2], v[3]);
+      if (base + src < chunks) part[2 * base + half * 32 + lane] = o;
+    }
+  }
+}
+
+// TMA-ring backward: CTA b owns the contiguous rows [b*R, min(M, (b+1)*R))
+// (fixed blocks keep the dweight sum order fixed); one thread streams each
+// row's inputs (dy, x, then dy2 and dres when present) into a ring of S
+// shared-memory stages, S rows ahead.  dweight partials stay in registers and
+// are written once per block, coalesced, like the register kernel above.
+template <int VPT, bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
+__global__ void __launch_bounds__(512)
+rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, int S, int* err) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ float2 slots[2][32];
+  __shared__ int s_abort;
+  constexpr int NIN = 2 + (HAS_DY2 ? 1 : 0) + (HAS_DRES ? 1 : 0);
+  const int row_bytes = N * 2;
+  const int stage_bytes = NIN * row_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * stage_bytes);
+  const int chunks = N >> 3;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+  const int64_t r1 = min(M, r0 + rows_per_block);
+  const float invN = 1.0f / static_cast<float>(N);
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < S; ++i) mbar_init(&bars[i], 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  int issued = 0;
+  auto issue = [&](int i) {
+    const int64_t row = r0 + i;
+    if (row >= r1) return;
+    unsigned char* st = smem + static_cast<size_t>(i % S) * stage_bytes;
+    uint64_t* bar = &bars[i % S];
+    const size_t off = static_cast<size_t>(row) * N;
+    mbar_arrive_expect_tx(bar, stage_bytes);
+    bulk_g2s(st, p.dy + off, row_bytes, bar);
+    bulk_g2s(st + row_bytes, p.x + off, row_bytes, bar);
+    int slot = 2;
+    if (HAS_DY2) bulk_g2s(st + (slot++) * row_bytes, p.dy2 + off, row_bytes, bar);
+    if (HAS_DRES) bulk_g2s(st + slot * row_bytes, p.dres + off, row_bytes, bar);
+    issued = i + 1;
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < S; ++i) issue(i);
+
+  float wf[VPT][8];
+  float acc[VPT][8];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int c = threadIdx.x + k * blockDim.x;
-    if (c < chunks) {
-      float4* dst = reinterpret_cast<float4*>(part + c * 8);
-      dst[0] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
-      dst[1] = make_float4(acc[k][4], acc[k][5], acc[k][6], acc[k][7]);
+    unpack8((c < chunks) ? ld_cached(p.w + c * 8) : make_uint4(0, 0, 0, 0), wf[k]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[k][e] = 0.f;
+  }
+  int parity = 0;
+  int i = 0;
+  for (; r0 + i < r1; ++i) {
+    const int64_t row = r0 + i;
+    const float rr = RECOMPUTE ? 0.f : __ldg(p.rstd + row);
+    const unsigned char* st = smem + static_cast<size_t>(i % S) * stage_bytes;
+    if (!mbar_wait(&bars[i % S], (i / S) & 1, err)) s_abort = 1;
+    uint4 gdy[VPT], gx[VPT], gdr[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      if (c < chunks) {
+        gdy[k] = *reinterpret_cast<const uint4*>(st + c * 16);
+        gx[k] = *reinterpret_cast<const uint4*>(st + row_bytes + c * 16);
+        if (HAS_DY2) {
+          // The summed gradient is a bf16 tensor in the reference graph.
+          float g[8], g2[8];
+          unpack8(gdy[k], g);
+          unpack8(*reinterpret_cast<const uint4*>(st + 2 * row_bytes + c * 16), g2);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) g[e] += g2[e];
+          gdy[k] = pack8(g);
+        }
+        if (HAS_DRES)
+          gdr[k] = *reinterpret_cast<const uint4*>(st + (HAS_DY2 ? 3 : 2) * row_bytes + c * 16);
+      } else {
+        gdy[k] = gx[k] = gdr[k] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      float g[8], xf[8];
+      unpack8(gdy[k], g);
+      unpack8(gx[k], xf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (RECOMPUTE) s1 = fmaf(xf[e], xf[e], s1);
+        s2 = fmaf(xf[e], g[e] * wf[k][e], s2);
+      }
+    }
+    const float2 tot = block_sum2(make_float2(s1, s2), slots, parity);
+    parity ^= 1;
+    if (s_abort) break;
+    if (threadIdx.x == 0) issue(i + S);  // stage i % S is free again
+    const float r = RECOMPUTE ? rsqrtf(tot.x * invN + eps) : rr;
+    const float cmean = r * tot.y * invN;  // mean(xhat * gw)
+    const size_t base = static_cast<size_t>(row) * N;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      float g[8], xf[8], o[8];
+      unpack8(gdy[k], g);
+      unpack8(gx[k], xf);
+      if (HAS_DRES) unpack8(gdr[k], o);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float xhat = xf[e] * r;
+        const float dx = (g[e] * wf[k][e] - xhat * cmean) * r;
+        acc[k][e] = fmaf(g[e], xhat, acc[k][e]);
+        o[e] = HAS_DRES ? o[e] + round_bf16(dx) : dx;
+      }
+      if (c < chunks) st_global(p.dx + base + c * 8, pack8(o));
+    }
+  }
+  if (threadIdx.x == 0 && s_abort)
+    for (int j = i; j < issued; ++j) mbar_wait(&bars[j % S], (j / S) & 1, nullptr);
+
+  float4* part = reinterpret_cast<float4*>(p.partials + static_cast<size_t>(blockIdx.x) * N);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int base = (threadIdx.x & ~31) + k * blockDim.x;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int src = half * 16 + (lane >> 1);
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __shfl_sync(0xffffffffu, acc[k][e], src);
+      const float4 o = (lane & 1) ? make_float4(v[4], v[5], v[6], v[7]) : make_float4(v[0], v[1], v[2], v[3]);
+      if (base + src < chunks) part[2 * base + half * 32 + lane] = o;
     }
   }
 }
@@ -361,53 +507,45 @@ rmsnorm_bwd_generic_dw(BwdIn p, int64_t M, int64_t N, int64_t rows_per_block) {
   p.partials[static_cast<size_t>(blockIdx.y) * N + col] = acc;
 }
 
-// dw[n] = sum_{b=0}^{G-1} partials[b, n]: warp w adds blocks w, w+8, ... in
-// order, then the 8 warp sums are added in warp order.  Fixed order, so the
-// result is bitwise reproducible.
-template <bool VEC>
-__global__ void __launch_bounds__(256)
+// dw[n] = sum_{b=0}^{G-1} partials[b, n].  A CTA owns 32 columns (one per
+// lane); warp w adds the blocks w, w+32, ... in order, then the 32 warp sums
+// of a column are added in warp order.  The order is fixed, so the result is
+// bitwise reproducible.  Each lane issues all of its (up to 16) loads before
+// the first add, so the kernel costs one memory round trip for G <= 512.
+__global__ void __launch_bounds__(1024)
 dw_reduce_kernel(const float* __restrict__ partials, int64_t G, int64_t N,
                  float* __restrict__ dw, uint16_t* __restrict__ dw_bf16) {
-  __shared__ float red[8][128];
+  __shared__ float red[32][33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * 128 + lane * 4;
-  float a[4] = {0.f, 0.f, 0.f, 0.f};
-  if (VEC) {
-    if (c0 < N) {
-      for (int64_t b = warp; b < G; b += 8) {
-        const float4 v = *reinterpret_cast<const float4*>(partials + b * N + c0);
-        a[0] += v.x; a[1] += v.y; a[2] += v.z; a[3] += v.w;
-      }
-    }
-  } else {
-    for (int64_t b = warp; b < G; b += 8) {
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  float a = 0.f;
+  if (col < N) {
+    for (int64_t b0 = warp; b0 < G; b0 += 32 * 16) {
+      float v[16];
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (c0 + j < N) a[j] += partials[b * N + c0 + j];
+      for (int j = 0; j < 16; ++j) {
+        const int64_t b = b0 + 32 * j;
+        v[j] = (b < G) ? __ldg(partials + b * N + col) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) a += v[j];
     }
   }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) red[warp][lane * 4 + j] = a[j];
+  red[warp][lane] = a;
   __syncthreads();
-  if (threadIdx.x < 128) {
-    const int64_t col = static_cast<int64_t>(blockIdx.x) * 128 + threadIdx.x;
-    if (col < N) {
-      float s = 0.f;
+  if (warp == 0 && col < N) {
+    float s = 0.f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) s += red[w][threadIdx.x];
-      if (dw) dw[col] = s;
-      if (dw_bf16) dw_bf16[col] = f_to_bf16(s);
-    }
+    for (int w = 0; w < 32; ++w) s += red[w][lane];
+    if (dw) dw[col] = s;
+    if (dw_bf16) dw_bf16[col] = f_to_bf16(s);
   }
 }
 
 int launch_dw_reduce(const float* partials, int64_t G, int64_t N, float* dw,
                      uint16_t* dw_bf16, cudaStream_t s) {
-  const dim3 grid(static_cast<unsigned>(ceil_div(N, 128)));
-  if (N % 4 == 0 && aligned16(partials))
-    dw_reduce_kernel<true><<<grid, 256, 0, s>>>(partials, G, N, dw, dw_bf16);
-  else
-    dw_reduce_kernel<false><<<grid, 256, 0, s>>>(partials, G, N, dw, dw_bf16);
+  const dim3 grid(static_cast<unsigned>(ceil_div(N, 32)));
+  dw_reduce_kernel<<<grid, 1024, 0, s>>>(partials, G, N, dw, dw_bf16);
   return check_launch();
 }
 
@@ -418,6 +556,8 @@ struct BwdPlan {
   RowCfg cfg;
   int64_t G;
   int64_t rows_per_block;
+  bool tma = false;  // TMA-ring kernel
+  int cps = 0;       // its CTAs per SM (same for every input set)
 };
 
 int vec_blocks_per_sm(int vpt, int threads) {
@@ -442,6 +582,23 @@ BwdPlan make_bwd_plan(int64_t M, int64_t N, bool aligned) {
   if (pl.cfg.vpt != 2) pl.cfg = RowCfg{0, 256};
   int sms = sm_count();
   if (sms <= 0) sms = 148;
+  if (pl.cfg.vpt == 2) {
+    // TMA ring: CTAs per SM from the register footprint of the heaviest input
+    // set (at most 2), the same for every input set (the stage count adapts),
+    // so the block count, and with it the partials layout, depends on M, N only.
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, rmsnorm_bwd_tma<2, true, true, true>,
+                                                      pl.cfg.threads, 0) != cudaSuccess) {
+      cudaGetLastError();
+      occ = 1;
+    }
+    pl.tma = true;
+    pl.cps = std::max(1, std::min(2, occ));
+    const int64_t target = std::max<int64_t>(1, std::min<int64_t>(M, static_cast<int64_t>(pl.cps) * sms));
+    pl.rows_per_block = ceil_div(M, target);
+    pl.G = ceil_div(M, pl.rows_per_block);
+    return pl;
+  }
   int64_t target = static_cast<int64_t>(sms) * vec_blocks_per_sm(pl.cfg.vpt, pl.cfg.threads);
   if (pl.cfg.vpt == 0) target = static_cast<int64_t>(sms) * 4;
   target = std::max<int64_t>(1, std::min<int64_t>(target, M));
@@ -459,6 +616,19 @@ template <bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
 int launch_bwd_t(const BwdPlan& pl, BwdIn p, int64_t M, int64_t N, float eps, cudaStream_t s) {
   const dim3 grid(static_cast<unsigned>(pl.G));
   const int T = pl.cfg.threads;
+  if (pl.tma) {
+    constexpr int NIN = 2 + (HAS_DY2 ? 1 : 0) + (HAS_DRES ? 1 : 0);
+    const int stage_bytes = NIN * static_cast<int>(N) * 2;
+    const int S = std::min(8, (220 * 1024 / pl.cps - 1024) / stage_bytes);
+    auto kern = rmsnorm_bwd_tma<2, HAS_DY2, HAS_DRES, RECOMPUTE>;
+    const int smem = std::max(S, 1) * stage_bytes + 8 * std::max(S, 1);
+    if (S >= 1 && allow_dynamic_smem(reinterpret_cast<const void*>(kern), smem)) {
+      kern<<<grid, T, smem, s>>>(p, M, static_cast<int>(N), eps, pl.rows_per_block, S,
+                                 device_error_word());
+      return check_launch();
+    }
+    return FRAG_ERR_SHAPE;
+  }
   switch (pl.cfg.vpt) {
     case 2:
       rmsnorm_bwd_vec<2, HAS_DY2, HAS_DRES, RECOMPUTE><<<grid, T, 0, s>>>(p, M, static_cast<int>(N), eps, pl.rows_per_block);

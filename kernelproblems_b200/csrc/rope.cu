@@ -12,9 +12,12 @@
 // The backward is the same rotation by the conjugate (v6/03d64c25b654/problem.py:12-43
 // multiplies the incoming gradient by conj(freqs_cis)).
 //
-// Vector path: one warp per token; D/16 lanes per head, each lane owns the 8
-// pairs with frequency indices 8j..8j+7, so its 8 (cos, sin) values are
-// computed once per token and reused for every head of q and k.
+// Vector path: one warp per token; D/16 lanes per head.  Lane j owns the two
+// 16-byte chunks at element offsets 8j and D/2 + 8j of every head, so each
+// load/store instruction of a warp covers contiguous 128-byte spans.  Those
+// chunks hold 8 rotation pairs: (x[8j+i], x[D/2+8j+i]) for neox, or the pairs
+// 4j..4j+3 and D/4+4j..D/4+4j+3 for the interleaved layout; the lane computes
+// their 8 (cos, sin) values once per token and reuses them for every head.
 #include <math.h>
 
 #include <algorithm>
@@ -69,7 +72,7 @@ __device__ __forceinline__ void rotate(const uint4& a, const uint4& c, const flo
       rc[i] = fc[i] * cs[i] + fa[i] * sn[i];
     }
   } else {
-    // a, c = x[16j..16j+16): pairs (re, im) at even/odd positions.
+    // a, c hold 4 (re, im) pairs each: a's use cs[0..3], c's use cs[4..7].
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float re = fa[2 * i], im = fa[2 * i + 1];
@@ -100,31 +103,35 @@ __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
   const int64_t pos = load_pos(p, b, s);
   const int j = lane % LPH, hs = lane / LPH;
 
+  // Frequency index of pair i (0..7) of this lane.
+  auto fidx = [&](int i) { return NEOX ? 8 * j + i : (i < 4 ? 4 * j + i : (half >> 1) + 4 * j + i - 4); };
   float cs[8], sn[8];
   if (TABLE) {
-    const float4* f = reinterpret_cast<const float4*>(p.freqs + 2 * (pos * p.fstride + 8 * j));
+    // pairs i = 0..3 and 4..7 are 4 consecutive complex values each
+    const float* row = p.freqs + 2 * pos * p.fstride;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 v = __ldg(f + i);
-      cs[2 * i] = v.x;
-      sn[2 * i] = v.y * p.sign;
-      cs[2 * i + 1] = v.z;
-      sn[2 * i + 1] = v.w * p.sign;
+    for (int h = 0; h < 2; ++h) {
+      const float4* f = reinterpret_cast<const float4*>(row + 2 * fidx(4 * h));
+      const float4 v0 = __ldg(f), v1 = __ldg(f + 1);
+      cs[4 * h + 0] = v0.x; sn[4 * h + 0] = v0.y * p.sign;
+      cs[4 * h + 1] = v0.z; sn[4 * h + 1] = v0.w * p.sign;
+      cs[4 * h + 2] = v1.x; sn[4 * h + 2] = v1.y * p.sign;
+      cs[4 * h + 3] = v1.z; sn[4 * h + 3] = v1.w * p.sign;
     }
   } else {
     const float fp = static_cast<float>(pos);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       float sv, cv;
-      sincosf(fp * sfreq[8 * j + i], &sv, &cv);
+      sincosf(fp * sfreq[fidx(i)], &sv, &cv);
       cs[i] = cv;
       sn[i] = sv * p.sign;
     }
   }
 
   // Element offsets of this lane's two 16-byte chunks within a head.
-  const int oa = NEOX ? 8 * j : 16 * j;
-  const int oc = NEOX ? half + 8 * j : 16 * j + 8;
+  const int oa = 8 * j;
+  const int oc = half + 8 * j;
 #pragma unroll
   for (int ti = 0; ti < 2; ++ti) {
     if (ti >= p.nt) break;

@@ -36,6 +36,54 @@ int sm_count() {
   return cache[d];
 }
 
+// Error word kernels report into (FRAG_DEVFLAG_* bits), one per device.
+__device__ int g_error_word;
+
+int* device_error_word() {
+  static std::mutex mu;
+  static int* cache[64] = {nullptr};
+  const int d = current_device();
+  if (d < 0 || d >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[d] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_error_word) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    cache[d] = static_cast<int*>(p);
+  }
+  return cache[d];
+}
+
+bool allow_dynamic_smem(const void* kernel, int bytes) {
+  // Largest dynamic shared memory size set so far, per device and kernel.
+  static std::mutex mu;
+  static const void* kern[64][32] = {};
+  static int set_bytes[64][32] = {};
+  const int d = current_device();
+  if (d < 0 || d >= 64) return false;
+  std::lock_guard<std::mutex> lk(mu);
+  int slot = -1;
+  for (int i = 0; i < 32; ++i) {
+    if (kern[d][i] == kernel) {
+      if (set_bytes[d][i] >= bytes) return true;
+      slot = i;
+      break;
+    }
+    if (kern[d][i] == nullptr && slot < 0) slot = i;
+  }
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (slot >= 0) {
+    kern[d][slot] = kernel;
+    set_bytes[d][slot] = bytes;
+  }
+  return true;
+}
+
 }  // namespace frag
 
 extern "C" {
@@ -60,5 +108,20 @@ const char* frag_status_string(int status) {
 int frag_last_cuda_error(void) { return frag::g_last_cuda_error; }
 
 int frag_device_sm_count(void) { return frag::sm_count(); }
+
+int frag_device_errors(int clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, frag::g_error_word, sizeof(int));
+  if (e == cudaSuccess && clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(frag::g_error_word, &zero, sizeof(int));
+  }
+  if (e != cudaSuccess) {
+    frag::set_last_cuda_error(e);
+    cudaGetLastError();
+    return -FRAG_ERR_CUDA;
+  }
+  return v;
+}
 
 }  // extern "C"

@@ -81,7 +81,18 @@ def _status_word(dev: torch.device) -> torch.Tensor:
 
 
 def check_status(device: torch.device | int | None = None) -> None:
-    """Synchronise and raise IndexError if a kernel flagged an out-of-range id."""
+    """Synchronise and raise IndexError if a kernel flagged an out-of-range id,
+    RuntimeError if a kernel gave up waiting for its own copies (a bounded
+    wait expired: its outputs are not valid)."""
+    lib = _lib.load()
+    cur = torch.cuda.current_device()
+    dev_idx = cur if device is None else (device if isinstance(device, int) else device.index)
+    with torch.cuda.device(dev_idx if dev_idx is not None else cur):
+        flags = lib.frag_device_errors(1)
+    if flags < 0:
+        raise FragError("frag_device_errors", -flags)
+    if flags & _lib.FRAG_DEVFLAG_WAIT_TIMEOUT:
+        raise RuntimeError("a libfrag kernel's bounded wait expired; its outputs are invalid")
     devs = list(_status_words) if device is None else [torch.device("cuda", device).index
                                                         if isinstance(device, int) else device.index]
     for idx in devs:
