@@ -49,6 +49,10 @@ NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 SUITE = ["C0F", "C2F", "C1B", "C3F", "C2B", "C3B", "C4F", "C4B"]
 DOMINANT = "C4B"  # largest share of the step; its main kernel is the roofline kernel
+# Fusions beyond the five configurations (SURVEY "next" rows), measured on request:
+#   C2N  embedding gather + RMSNorm fused (C2 ids/table, eps 1e-5)
+#   C3S  RoPE fwd writing q/k in the [B, H, S, D] layout attention reads (C3 shapes)
+NEXT = ["C2N", "C3S"]
 
 
 # ------------------------------------------------------------------ helpers
@@ -60,7 +64,7 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="suite",
-                    help="suite | emb_vp | one fragment of " + ",".join(SUITE))
+                    help="suite | next | emb_vp | one fragment of " + ",".join(SUITE + NEXT))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -307,7 +311,7 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
         f.e2e = lambda h: _e2e_call(lambda xs: ops.rmsnorm_fwd(xs["x"], w, c.eps), h)
         return f
 
-    def mk_rms_bwd(name, c, with_dres, s):
+    def mk_rms_bwd(name, c, with_dres, s, split_stages):
         w = cf.rmsnorm_weight(c.N, device=dev, seed=seed0 + s)
         x = cf.randn(c.shape, device=dev, seed=seed0 + s + 1)
         g = cf.randn(c.shape, device=dev, seed=seed0 + s + 2)
@@ -320,11 +324,24 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
         dwg = torch.empty(c.N, dtype=torch.float32, device=dev)
         pbuf = torch.empty(world, c.N, dtype=torch.float32, device=dev)
         nb = cf.bytes_add_rmsnorm_bwd(c.M, c.N) if with_dres else cf.bytes_rmsnorm_bwd(c.M, c.N)
-        f = Frag(name, c.name + (" bwd" if with_dres else ""), c.M, nb,
-                 [("rmsnorm_bwd_main", lambda: ops.rmsnorm_bwd(g, x, r, w, dres=dh, dw_dtype=None,
-                                                              workspace=ws)),
-                  ("dw_reduce", lambda: ops.dw_reduce(parts, out=dw))],
-                 exchange=exchange_dw(dw, dwg, pbuf))
+        if split_stages:
+            # row kernel and dweight reduce as two timed stages (the row kernel
+            # is the roofline kernel)
+            stages = [("rmsnorm_bwd_main", lambda: ops.rmsnorm_bwd(g, x, r, w, dres=dh, dw_dtype=None,
+                                                                  workspace=ws)),
+                      ("dw_reduce", lambda: ops.dw_reduce(parts, out=dw))]
+            f = Frag(name, c.name + (" bwd" if with_dres else ""), c.M, nb, stages,
+                     exchange=exchange_dw(dw, dwg, pbuf))
+        else:
+            # one call, as a user makes it: row kernel + dependent dweight reduce
+            holder = {}
+
+            def one():
+                holder["dx"], holder["dw"] = ops.rmsnorm_bwd(g, x, r, w, dres=dh, workspace=ws)
+            one()  # holder["dw"] exists before the exchange is built
+            f = Frag(name, c.name + (" bwd" if with_dres else ""), c.M, nb, [("rmsnorm_bwd", one)],
+                     exchange=(None if world == 1 else
+                               (lambda: exchange_dw(holder["dw"], dwg, pbuf)())))
         f.host = dict(g=g, x=x, r=r) if dh is None else dict(g=g, x=x, r=r, dh=dh)
         f.e2e = lambda h: _e2e_call(lambda xs: ops.rmsnorm_bwd(xs["g"], xs["x"], xs["r"], w,
                                                                dres=xs.get("dh")), h)
@@ -379,11 +396,39 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
         f.e2e = lambda h_: _e2e_call(lambda xs: ops.add_rmsnorm_fwd(xs["res"], xs["x"], w, c.eps), h_)
         return f
 
-    builders = {"C0F": mk_c0f, "C1B": lambda: mk_rms_bwd("C1B", C1, False, 3),
+    def mk_c2n():
+        # embedding gather fused with RMSNorm (the first attention_norm), C2 shapes
+        c = C2
+        ids = cf.embedding_ids(c, device=dev, seed=2 + rank)
+        table = cf.randn((c.vocab, c.dim), std=0.02, device=dev, seed=seed0 + 7)
+        w = cf.rmsnorm_weight(c.dim, device=dev, seed=seed0 + 9)
+        f = Frag("C2N", c.name + " fwd + RMSNorm fused", c.T,
+                 cf.bytes_embedding_fwd(c.T, c.dim) + c.dim * cf.BF16,
+                 [("embedding_rmsnorm_fwd", lambda: ops.embedding_rmsnorm_fwd(ids, table, w, 1e-5))])
+        f.host = dict(ids=ids)
+        f.e2e = lambda h: _e2e_call(lambda xs: ops.embedding_rmsnorm_fwd(xs["ids"], table, w, 1e-5)[0], h)
+        return f
+
+    def mk_c3s():
+        # RoPE fwd writing the [B, H, S, D] layout attention reads, C3 shapes
+        c = C3
+        pos = cf.rope_positions(c, device=dev)
+        q = cf.randn((c.B, c.S, c.Hq, c.D), device=dev, seed=seed0 + 15)
+        k = cf.randn((c.B, c.S, c.Hk, c.D), device=dev, seed=seed0 + 16)
+        oq = torch.empty((c.B, c.Hq, c.S, c.D), dtype=q.dtype, device=dev).transpose(1, 2)
+        ok = torch.empty((c.B, c.Hk, c.S, c.D), dtype=k.dtype, device=dev).transpose(1, 2)
+        f = Frag("C3S", c.name + " fwd into [B,H,S,D]", c.T, cf.bytes_rope(c.T, c.Hq, c.Hk, c.D),
+                 [("rope_bhsd", lambda: ops.rope(q, k, pos, theta=c.theta, out_q=oq, out_k=ok))])
+        f.host = dict(q=q, k=k)
+        f.e2e = lambda h: _e2e_call(lambda xs: ops.rope(xs["q"], xs["k"], pos, theta=c.theta,
+                                                        out_layout="bhsd"), h)
+        return f
+
+    builders = {"C2N": mk_c2n, "C3S": mk_c3s, "C0F": mk_c0f, "C1B": lambda: mk_rms_bwd("C1B", C1, False, 3, False),
                 "C2F": lambda: mk_c2("C2F"), "C2B": lambda: mk_c2("C2B"),
                 "C3F": lambda: mk_c3("C3F"), "C3B": lambda: mk_c3("C3B"),
-                "C4F": mk_c4f, "C4B": lambda: mk_rms_bwd("C4B", C4, True, 23)}
-    return [builders[n]() for n in SUITE if n in names]
+                "C4F": mk_c4f, "C4B": lambda: mk_rms_bwd("C4B", C4, True, 23, True)}
+    return [builders[n]() for n in SUITE + NEXT if n in names]
 
 
 def _e2e_call(fn, host):
@@ -566,7 +611,7 @@ def ours_arm(args, rank, local_rank, world):
     _lib.load()
     if args.workload == "emb_vp":
         return emb_vp_arm(args, rank, world, dev, pg)
-    names = SUITE if args.workload == "suite" else [args.workload]
+    names = {"suite": SUITE, "next": NEXT}.get(args.workload, [args.workload])
     frags = build_suite(dev, world, rank, names, pg, args.rows_frac)
     step = Step(frags, not args.no_graphs)
     step_bytes = sum(f.bytes for f in frags)
@@ -597,6 +642,9 @@ def ours_arm(args, rank, local_rank, world):
     frag_ms = {f.name: [] for f in frags}
     stage_ms = {f.name: [[] for _ in f.stages] for f in frags}
     for _ in range(R):
+        if world > 1:
+            dist.barrier()  # start every breakdown replay together, so no rank's
+            torch.cuda.synchronize()  # exchange absorbs another rank's skew
         step.run()
         torch.cuda.synchronize()
         for name, (fm, st) in step.breakdown().items():

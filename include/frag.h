@@ -180,6 +180,23 @@ FRAG_API int frag_embedding_fwd(const int64_t* ids, const void* table, void* out
                        frag_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
+ * Token-embedding gather fused with RMSNorm.
+ *   e = table[ids[t]];  rstd[t] = 1/sqrt(mean(e^2) + eps);  y[t] = bf16((e*rstd)*w)
+ * The gathered row is normalised in registers; it is also written to emb_out
+ * (bit exact) when emb_out is not NULL.  Ids outside [0, V) give zero rows
+ * and set FRAG_DEVFLAG_INDEX_OOB in *status.
+ * Replaces aten.embedding -> aten._fused_rms_norm of v8/12545c1e9b06/problem.py:16-51
+ * (drop-in v8/12545c1e9b06/optimized_kernel.py:66, whose Triton kernel
+ * `_embedding_rmsnorm_kernel` is at :7).
+ * ids: int64 [T]; table: bf16 [V, D]; w: bf16 [D]; y, emb_out: bf16 [T, D];
+ * rstd: fp32 [T] or NULL.
+ * ------------------------------------------------------------------------- */
+FRAG_API int frag_embedding_rmsnorm_fwd(const int64_t* ids, const void* table, const void* w,
+                                        void* y, float* rstd, void* emb_out, int64_t T,
+                                        int64_t V, int64_t D, float eps, int32_t* status,
+                                        frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
  * Token-embedding backward into an fp32 table gradient (deterministic).
  *   G[v,:] = sum over t in increasing order with ids[t]-vocab_lo == v and
  *            ids[t] != padding_idx of grad[t,:]      (fp32 accumulation)

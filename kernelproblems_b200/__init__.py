@@ -18,6 +18,7 @@ from .ops import (  # noqa: F401
     dw_reduce,
     embedding_bwd,
     embedding_fwd,
+    embedding_rmsnorm_fwd,
     rmsnorm_bwd,
     rmsnorm_fwd,
     rope,

@@ -80,6 +80,8 @@ SIGNATURES: dict[str, tuple] = {
     "frag_rmsnorm_bwd_num_blocks": (_i64, [_i64, _i64]),
     "frag_dw_reduce": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "frag_embedding_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "frag_embedding_rmsnorm_fwd": (
+        _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
     "frag_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64]),
     "frag_embedding_bwd": (
         _int,

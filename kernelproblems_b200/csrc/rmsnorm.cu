@@ -102,6 +102,108 @@ rmsnorm_fwd_vec(const uint16_t* __restrict__ x, const uint16_t* __restrict__ res
   }
 }
 
+// Embedding gather fused with RMSNorm (v8/12545c1e9b06/problem.py:16-51:
+// aten.embedding -> aten._fused_rms_norm): the row is read from
+// table[ids[row]] and normalised in registers, so the gathered embedding is
+// written only when the caller asks for it.  Ids outside [0, V) give a zero
+// row and set FRAG_DEVFLAG_INDEX_OOB.
+template <int VPT, bool WRITE_EMB, bool WRITE_RSTD>
+__global__ void __launch_bounds__(512)
+emb_rmsnorm_fwd_vec(const int64_t* __restrict__ ids, const uint16_t* __restrict__ table,
+                    const uint16_t* __restrict__ w, uint16_t* __restrict__ emb,
+                    uint16_t* __restrict__ y, float* __restrict__ rstd, int64_t V, int N,
+                    float eps, int32_t* status) {
+  __shared__ float slots[2][32];
+  const int chunks = N >> 3;
+  const int64_t row = blockIdx.x;
+  const int64_t id = __ldg(ids + row);
+  const bool ok = id >= 0 && id < V;
+  if (!ok && threadIdx.x == 0 && status) atomicOr(status, FRAG_DEVFLAG_INDEX_OOB);
+  const uint16_t* src = table + (ok ? id : 0) * static_cast<int64_t>(N);
+  const size_t base = static_cast<size_t>(row) * N;
+  uint4 xv[VPT], wv[VPT];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    xv[k] = (ok && c < chunks) ? ld_stream(src + c * 8) : make_uint4(0, 0, 0, 0);
+    wv[k] = (c < chunks) ? ld_cached(w + c * 8) : make_uint4(0, 0, 0, 0);
+  }
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (WRITE_EMB && c < chunks) st_global(emb + base + c * 8, xv[k]);
+    unpack8(xv[k], v[k]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[k][i], v[k][i], ss);
+  }
+  const float tot = block_sum(ss, slots, 0);
+  const float r = rsqrtf(tot / static_cast<float>(N) + eps);
+  if (WRITE_RSTD && threadIdx.x == 0) rstd[row] = r;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < chunks) {
+      float wf[8], o[8];
+      unpack8(wv[k], wf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = (v[k][i] * r) * wf[i];
+      st_global(y + base + c * 8, pack8(o));
+    }
+  }
+}
+
+template <bool WRITE_EMB, bool WRITE_RSTD>
+__global__ void __launch_bounds__(256)
+emb_rmsnorm_fwd_generic(const int64_t* __restrict__ ids, const uint16_t* __restrict__ table,
+                        const uint16_t* __restrict__ w, uint16_t* __restrict__ emb,
+                        uint16_t* __restrict__ y, float* __restrict__ rstd, int64_t V, int64_t N,
+                        float eps, int32_t* status) {
+  __shared__ float slots[2][32];
+  const int64_t row = blockIdx.x;
+  const int64_t id = ids[row];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && threadIdx.x == 0 && status) atomicOr(status, FRAG_DEVFLAG_INDEX_OOB);
+  const uint16_t* src = table + (ok ? id : 0) * N;
+  const size_t base = static_cast<size_t>(row) * N;
+  float ss = 0.f;
+  for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+    const uint16_t u = ok ? src[n] : static_cast<uint16_t>(0);
+    if (WRITE_EMB) emb[base + n] = u;
+    const float v = bf16_to_f(u);
+    ss = fmaf(v, v, ss);
+  }
+  const float tot = block_sum(ss, slots, 0);
+  const float r = rsqrtf(tot / static_cast<float>(N) + eps);
+  if (WRITE_RSTD && threadIdx.x == 0) rstd[row] = r;
+  for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+    const float v = ok ? bf16_to_f(src[n]) : 0.f;
+    y[base + n] = f_to_bf16((v * r) * bf16_to_f(w[n]));
+  }
+}
+
+template <bool WRITE_EMB, bool WRITE_RSTD>
+int launch_emb_rms_t(const RowCfg& cfg, const int64_t* ids, const uint16_t* table, const uint16_t* w,
+                     uint16_t* emb, uint16_t* y, float* rstd, int64_t T, int64_t V, int64_t N,
+                     float eps, int32_t* status, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(T));
+  switch (cfg.vpt) {
+    case 2:
+      emb_rmsnorm_fwd_vec<2, WRITE_EMB, WRITE_RSTD><<<grid, cfg.threads, 0, s>>>(
+          ids, table, w, emb, y, rstd, V, static_cast<int>(N), eps, status);
+      break;
+    case 4:
+      emb_rmsnorm_fwd_vec<4, WRITE_EMB, WRITE_RSTD><<<grid, cfg.threads, 0, s>>>(
+          ids, table, w, emb, y, rstd, V, static_cast<int>(N), eps, status);
+      break;
+    default:
+      emb_rmsnorm_fwd_generic<WRITE_EMB, WRITE_RSTD><<<grid, 256, 0, s>>>(ids, table, w, emb, y, rstd, V, N,
+                                                                           eps, status);
+  }
+  return check_launch();
+}
+
 template <bool HAS_RES, bool WRITE_H, bool WRITE_RSTD>
 __global__ void __launch_bounds__(256)
 rmsnorm_fwd_generic(const uint16_t* __restrict__ x, const uint16_t* __restrict__ res,
@@ -329,6 +431,9 @@ rmsnorm_bwd_vec(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block) {
 template <int VPT, bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
 __global__ void __launch_bounds__(512)
 rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, int S, int* err) {
+  // The dweight reduce that follows may be launched now; it waits for this
+  // grid to finish before reading the partials.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ float2 slots[2][32];
   __shared__ int s_abort;
@@ -516,6 +621,9 @@ __global__ void __launch_bounds__(1024)
 dw_reduce_kernel(const float* __restrict__ partials, int64_t G, int64_t N,
                  float* __restrict__ dw, uint16_t* __restrict__ dw_bf16) {
   __shared__ float red[32][33];
+  // Launched as a programmatic dependent of the row kernel: wait until that
+  // grid has completed and its partials are visible (no-op otherwise).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t col = static_cast<int64_t>(blockIdx.x) * 32 + lane;
   float a = 0.f;
@@ -543,10 +651,20 @@ dw_reduce_kernel(const float* __restrict__ partials, int64_t G, int64_t N,
 }
 
 int launch_dw_reduce(const float* partials, int64_t G, int64_t N, float* dw,
-                     uint16_t* dw_bf16, cudaStream_t s) {
-  const dim3 grid(static_cast<unsigned>(ceil_div(N, 32)));
-  dw_reduce_kernel<<<grid, 1024, 0, s>>>(partials, G, N, dw, dw_bf16);
-  return check_launch();
+                     uint16_t* dw_bf16, cudaStream_t s, bool after_row_kernel = false) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(ceil_div(N, 32)));
+  cfg.blockDim = dim3(1024);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  // Directly behind the row kernel: a programmatic dependent launch, so its
+  // launch overlaps that kernel's tail.
+  cfg.attrs = attr;
+  cfg.numAttrs = after_row_kernel ? 1 : 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, dw_reduce_kernel, partials, G, N, dw, dw_bf16));
 }
 
 // Row-block plan shared by the workspace query and the launch: the number of
@@ -587,8 +705,13 @@ BwdPlan make_bwd_plan(int64_t M, int64_t N, bool aligned) {
     // set (at most 2), the same for every input set (the stage count adapts),
     // so the block count, and with it the partials layout, depends on M, N only.
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, rmsnorm_bwd_tma<2, true, true, true>,
-                                                      pl.cfg.threads, 0) != cudaSuccess) {
+    const cudaError_t oe =
+        pl.cfg.vpt == 1
+            ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, rmsnorm_bwd_tma<1, true, true, true>,
+                                                            pl.cfg.threads, 0)
+            : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, rmsnorm_bwd_tma<2, true, true, true>,
+                                                            pl.cfg.threads, 0);
+    if (oe != cudaSuccess) {
       cudaGetLastError();
       occ = 1;
     }
@@ -620,7 +743,8 @@ int launch_bwd_t(const BwdPlan& pl, BwdIn p, int64_t M, int64_t N, float eps, cu
     constexpr int NIN = 2 + (HAS_DY2 ? 1 : 0) + (HAS_DRES ? 1 : 0);
     const int stage_bytes = NIN * static_cast<int>(N) * 2;
     const int S = std::min(8, (220 * 1024 / pl.cps - 1024) / stage_bytes);
-    auto kern = rmsnorm_bwd_tma<2, HAS_DY2, HAS_DRES, RECOMPUTE>;
+    auto kern = pl.cfg.vpt == 1 ? rmsnorm_bwd_tma<1, HAS_DY2, HAS_DRES, RECOMPUTE>
+                                : rmsnorm_bwd_tma<2, HAS_DY2, HAS_DRES, RECOMPUTE>;
     const int smem = std::max(S, 1) * stage_bytes + 8 * std::max(S, 1);
     if (S >= 1 && allow_dynamic_smem(reinterpret_cast<const void*>(kern), smem)) {
       kern<<<grid, T, smem, s>>>(p, M, static_cast<int>(N), eps, pl.rows_per_block, S,
@@ -734,7 +858,7 @@ int frag_rmsnorm_bwd(const void* dy, const void* dy2, const void* x, const float
   }
   if (st != FRAG_OK) return st;
   if (dw || dw_bf16)
-    return launch_dw_reduce(p.partials, pl.G, N, dw, static_cast<uint16_t*>(dw_bf16), s);
+    return launch_dw_reduce(p.partials, pl.G, N, dw, static_cast<uint16_t*>(dw_bf16), s, pl.tma);
   return FRAG_OK;
 }
 
@@ -794,4 +918,27 @@ extern "C" int frag_rmsnorm_bwd_noalloc(const void* dy, const void* dy2, const v
   if (st != FRAG_OK) return st;
   return frag_rmsnorm_bwd(dy, dy2, x, rstd, w, dres, dx_out, dw, dw_bf16, M, N, eps, ws,
                           FRAG_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+extern "C" int frag_embedding_rmsnorm_fwd(const int64_t* ids, const void* table, const void* w,
+                                          void* y, float* rstd, void* emb_out, int64_t T,
+                                          int64_t V, int64_t D, float eps, int32_t* status,
+                                          frag_stream_t stream) {
+  if (T < 0 || V < 0 || D < 0) return FRAG_ERR_INVALID_ARG;
+  if (T == 0) return FRAG_OK;
+  if (D == 0 || T > 0x7fffffffLL) return FRAG_ERR_SHAPE;
+  if (!ids || !w || !y || (V > 0 && !table)) return FRAG_ERR_INVALID_ARG;
+  bool aligned = aligned16(w) && aligned16(y) && (V == 0 || aligned16(table));
+  if (emb_out) aligned = aligned && aligned16(emb_out);
+  const RowCfg cfg = pick_row_cfg(D, aligned);
+  auto tab = static_cast<const uint16_t*>(table);
+  auto W = static_cast<const uint16_t*>(w);
+  auto E = static_cast<uint16_t*>(emb_out);
+  auto Y = static_cast<uint16_t*>(y);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (emb_out)
+    return rstd ? launch_emb_rms_t<true, true>(cfg, ids, tab, W, E, Y, rstd, T, V, D, eps, status, s)
+                : launch_emb_rms_t<true, false>(cfg, ids, tab, W, E, Y, rstd, T, V, D, eps, status, s);
+  return rstd ? launch_emb_rms_t<false, true>(cfg, ids, tab, W, E, Y, rstd, T, V, D, eps, status, s)
+              : launch_emb_rms_t<false, false>(cfg, ids, tab, W, E, Y, rstd, T, V, D, eps, status, s);
 }

@@ -30,6 +30,7 @@ __all__ = [
     "rmsnorm_bwd_num_blocks",
     "dw_reduce",
     "embedding_fwd",
+    "embedding_rmsnorm_fwd",
     "embedding_bwd",
     "rope",
     "check_status",
@@ -272,6 +273,34 @@ def embedding_fwd(ids: torch.Tensor, table: torch.Tensor, *, vocab_lo: int = 0,
     return o
 
 
+def embedding_rmsnorm_fwd(ids: torch.Tensor, table: torch.Tensor, weight: torch.Tensor,
+                          eps: float = 1e-5, *, save_rstd: bool = False,
+                          return_embedding: bool = False):
+    """y = rmsnorm(table[ids]) * weight without writing the gathered rows to
+    HBM (unless return_embedding).  Returns (y, rstd or None, emb or None)."""
+    _need(ids, "ids", torch.int64)
+    _need(table, "table", torch.bfloat16, ids.device)
+    _need(weight, "weight", torch.bfloat16, ids.device)
+    if table.dim() != 2 or not table.is_contiguous():
+        raise ValueError("table must be a contiguous [rows, D] tensor")
+    V, D = table.shape
+    if weight.numel() != D:
+        raise ValueError(f"weight has {weight.numel()} elements, table rows have {D}")
+    ids_c = ids.contiguous()
+    T = ids_c.numel()
+    y = torch.empty(*ids.shape, D, dtype=torch.bfloat16, device=ids.device)
+    rstd = torch.empty(ids.shape, dtype=torch.float32, device=ids.device) if save_rstd else None
+    emb = torch.empty_like(y) if return_embedding else None
+    wc = weight.contiguous()
+    with _on_device(ids.device):
+        st = _status_word(ids.device)
+        _lib.call("frag_embedding_rmsnorm_fwd", _ptr(ids_c), _ptr(table), _ptr(wc), _ptr(y), _ptr(rstd),
+                  _ptr(emb), T, V, D, float(eps), _ptr(st), _stream(ids.device))
+    if _SYNC_CHECK:
+        check_status(ids.device)
+    return y, rstd, emb
+
+
 def embedding_bwd(grad: torch.Tensor, ids: torch.Tensor, num_rows: int, *, vocab_lo: int = 0,
                   vocab_total: int | None = None, padding_idx: int = -1,
                   out: torch.Tensor | None = None,
@@ -323,10 +352,19 @@ def _rope_desc(x: torch.Tensor, out: torch.Tensor, name: str) -> _lib.RopeTensor
                            out.stride(0), out.stride(1), out.stride(2))
 
 
+def _new_out(x: torch.Tensor, out_layout: str) -> torch.Tensor:
+    B, S, H, D = x.shape
+    if out_layout == "bshd":
+        return torch.empty((B, S, H, D), dtype=x.dtype, device=x.device)
+    if out_layout == "bhsd":  # [B, H, S, D] storage, returned as a [B, S, H, D] view
+        return torch.empty((B, H, S, D), dtype=x.dtype, device=x.device).transpose(1, 2)
+    raise ValueError("out_layout must be 'bshd' or 'bhsd'")
+
+
 def rope(q: torch.Tensor, k: torch.Tensor | None = None, positions: torch.Tensor | None = None, *,
          theta: float | None = 500000.0, freqs: torch.Tensor | None = None,
          layout: str = "neox", inverse: bool = False, out_q: torch.Tensor | None = None,
-         out_k: torch.Tensor | None = None):
+         out_k: torch.Tensor | None = None, out_layout: str = "bshd"):
     """Rotary embedding of q (and k) given as [B, S, H, D] views (any strides,
     contiguous head dim).  Returns (out_q, out_k); outputs default to new
     contiguous tensors and may alias the inputs (in-place).
@@ -335,20 +373,23 @@ def rope(q: torch.Tensor, k: torch.Tensor | None = None, positions: torch.Tensor
     position = s.  freqs: complex64 [P, D/2] table indexed by position (the
     reference's freqs_cis input); without it cos/sin are computed in
     registers from theta.  inverse=True applies the conjugate rotation (the
-    backward)."""
+    backward).  out_layout="bhsd" writes new outputs in the [B, H, S, D]
+    storage order attention kernels read (the transpose is fused into the
+    stores; the returned tensors are [B, S, H, D] views of that storage, so
+    `.transpose(1, 2)` gives contiguous [B, H, S, D])."""
     _need(q, "q", torch.bfloat16)
     dev = q.device
     if layout not in _LAYOUTS:
         raise ValueError(f"layout must be one of {sorted(_LAYOUTS)}")
     B, S, Hq, D = q.shape
-    oq = torch.empty(q.shape, dtype=q.dtype, device=dev) if out_q is None else out_q
+    oq = _new_out(q, out_layout) if out_q is None else out_q
     descs = [_rope_desc(q, oq, "q")]
     ok = None
     if k is not None:
         _need(k, "k", torch.bfloat16, dev)
         if k.shape[0] != B or k.shape[1] != S or k.shape[3] != D:
             raise ValueError(f"k {tuple(k.shape)} does not match q {tuple(q.shape)}")
-        ok = torch.empty(k.shape, dtype=k.dtype, device=dev) if out_k is None else out_k
+        ok = _new_out(k, out_layout) if out_k is None else out_k
         descs.append(_rope_desc(k, ok, "k"))
     arr = (_lib.RopeTensor * len(descs))(*descs)
     pos_ptr, pos_dtype, psb, pss = None, _lib.FRAG_POS_NONE, 0, 0

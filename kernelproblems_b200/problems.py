@@ -207,7 +207,41 @@ def rope_bwd_03d64c25b654(_conj_62, getitem_642):
     return _rope_bwd_strided(getitem_642, _conj_62)
 
 
+# ------------------------------------------------- SURVEY "next" fusions
+
+_SPLITS_873 = [512, 2097152, 524288, 524288, 2097152, 512, 7340032, 7340032, 7340032]
+_SHAPES_873 = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (4096,), (14336, 4096)]
+
+
+def emb_rms_12545c1e9b06(wait_tensor_871, arg583_1, wait_tensor_873):
+    """v8/12545c1e9b06/optimized_kernel.py:66: embedding gather fused with the
+    first attention_norm RMSNorm (eps 1e-5), the norm weight taken from split 0
+    of the second FSDP buffer (problem.py:27-39); the gathered rows are never
+    written to HBM.  Also returns the contiguous copies of splits 1-6 the graph
+    makes (FSDP unshard copies: plain data movement, done with torch)."""
+    table = wait_tensor_871.view(VOCAB, DIM)
+    parts = wait_tensor_873.view(8, -1).split(_SPLITS_873, dim=1)
+    w = parts[0].contiguous().view(-1)
+    y, _, _ = ops.embedding_rmsnorm_fwd(arg583_1, table, w, 1e-5)
+    y2 = y.view(-1, DIM)
+    clones = [parts[i + 1].contiguous().view(_SHAPES_873[i]) for i in range(6)]
+    return (y2, y2, y2, *clones)
+
+
+def rope_sdpa_6b92d6e665ab(arg586_1, arg582_1, mm_217, mm_218):
+    """v4/6b92d6e665ab/optimized_kernel.py: q and k RoPE returned as the
+    [1, H, S, 128] transposed views attention consumes; the reference graph
+    computes each twice, so two independent results are returned too."""
+    S = mm_217.shape[0]
+    pos = arg586_1.view(1, S)
+    q, k = ops.rope(_heads(mm_217, S), _heads(mm_218, S), pos, freqs=arg582_1, layout="interleaved")
+    q2, k2 = ops.rope(_heads(mm_217, S), _heads(mm_218, S), pos, freqs=arg582_1, layout="interleaved")
+    return (q.transpose(1, 2), k.transpose(1, 2), q2.transpose(1, 2), k2.transpose(1, 2))
+
+
 PROBLEMS: dict[str, Callable] = {
+    "v8/12545c1e9b06": emb_rms_12545c1e9b06,
+    "v4/6b92d6e665ab": rope_sdpa_6b92d6e665ab,
     "v8/f4e9e58fef73": rms_fwd_f4e9e58fef73,
     "v7/f4e9e58fef73": rms_fwd_f4e9e58fef73,
     "v8/4b90e2d83144": rms_fwd_4b90e2d83144,

@@ -109,6 +109,11 @@ def embedding_fwd_vocab_shard(table_shard: torch.Tensor, ids: torch.Tensor, voca
         *ids.shape, table_shard.shape[1], dtype=table_shard.dtype)
 
 
+def embedding_rmsnorm_fwd(table: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, eps: float):
+    """aten.embedding -> aten._fused_rms_norm (v8/12545c1e9b06/problem.py:24,39)."""
+    return aten._fused_rms_norm.default(aten.embedding.default(table, ids), [w.numel()], w, eps)
+
+
 def embedding_bwd(grad: torch.Tensor, ids: torch.Tensor, num_weights: int,
                   padding_idx: int = -1) -> torch.Tensor:
     """aten.embedding_dense_backward -> _to_copy(fp32) (v7/a12a160cb11b/problem.py:16,19).

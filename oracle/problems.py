@@ -141,7 +141,38 @@ def rope_bwd_03d64c25b654(conj_freqs, g):
     return _rope_bwd(g, aten.clone.default(conj_freqs))
 
 
+SPLITS_873 = [512, 2097152, 524288, 524288, 2097152, 512, 7340032, 7340032, 7340032]
+SHAPES_873 = [[4096, 4096], [1024, 4096], [1024, 4096], [4096, 4096], [4096], [14336, 4096]]
+
+
+def emb_rms_12545c1e9b06(flat871, ids, flat873):
+    """v8/12545c1e9b06/problem.py:16-102: embedding of the FSDP table buffer,
+    RMSNorm with the weight gathered from split 0 of the second buffer, plus
+    contiguous clones of splits 1-6."""
+    table = flat871.view(128256, 4096)
+    parts = aten.split_with_sizes.default(flat873.view(8, -1), SPLITS_873, 1)
+    w = aten._unsafe_view.default(aten.clone.default(parts[0], memory_format=torch.contiguous_format), [4096])
+    y, _ = F.embedding_rmsnorm_fwd(table, ids, w, 1e-5)
+    y2 = y.view(8192, 4096)
+    clones = [aten._unsafe_view.default(aten.clone.default(parts[i + 1], memory_format=torch.contiguous_format),
+                                        SHAPES_873[i]) for i in range(6)]
+    return (y2, y2, y2, *clones)
+
+
+def rope_sdpa_6b92d6e665ab(pos, freqs, mm_217, mm_218):
+    """v4/6b92d6e665ab/problem.py: q and k RoPE (each computed twice), returned
+    as [1, H, S, 128] transposed views."""
+    f = aten.index.Tensor(freqs, [aten.squeeze.dim(pos, 0)])
+    q = _rope_rows(mm_217, 8192, f)
+    k = _rope_rows(mm_218, 8192, f)
+    q2 = _rope_rows(mm_217, 8192, f)
+    k2 = _rope_rows(mm_218, 8192, f)
+    return (q.transpose(1, 2), k.transpose(1, 2), q2.transpose(1, 2), k2.transpose(1, 2))
+
+
 ORACLES = {
+    "v8/12545c1e9b06": emb_rms_12545c1e9b06,
+    "v4/6b92d6e665ab": rope_sdpa_6b92d6e665ab,
     "v8/f4e9e58fef73": rms_fwd_f4e9e58fef73,
     "v7/f4e9e58fef73": rms_fwd_f4e9e58fef73,
     "v8/4b90e2d83144": rms_fwd_4b90e2d83144,
