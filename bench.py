@@ -199,8 +199,10 @@ class Frag:
 
 class Step:
     """The suite step.  Fragments are captured into CUDA graphs, one graph per
-    run of fragments between NCCL exchanges (the whole step at N=1), with
-    timing events recorded inside the graphs (external event nodes)."""
+    run of fragments between NCCL exchanges (the whole step at N=1).  Two
+    graph sets are captured: a plain one, replayed in the timed region, and an
+    instrumented one with timing events recorded between fragments and stages
+    (external event nodes), replayed only for the per-fragment breakdown."""
 
     def __init__(self, frags, use_graphs: bool):
         self.frags = frags
@@ -216,48 +218,63 @@ class Step:
                 cur = []
         if cur:
             segs.append(cur)
-        self.segments = []
         self.use_graphs = use_graphs
+        self.plain, self.timed = [], []
+        n_nodes = 0
         for seg in segs:
             for f in seg:
                 f.ev = [torch.cuda.Event(enable_timing=True, external=use_graphs)
                         for _ in range(len(f.stages) + 1)]
                 f.ev_end = torch.cuda.Event(enable_timing=True) if f.exchange is not None else None
-            g = None
+            gp = gt = None
             if use_graphs:
-                g = torch.cuda.CUDAGraph(keep_graph=True)
-                with torch.cuda.graph(g, capture_error_mode="thread_local"):
-                    self._launch(seg)
-                n = count_kernel_nodes(g)
-                for f in seg:
-                    f.kernel_nodes = 0
-                seg[0].kernel_nodes = max(n, 0)  # per segment; summed below
-                g.instantiate()
-            self.segments.append((g, seg))
+                gp = torch.cuda.CUDAGraph(keep_graph=True)
+                with torch.cuda.graph(gp, capture_error_mode="thread_local"):
+                    self._launch(seg, events=False)
+                n_nodes += max(count_kernel_nodes(gp), 0)
+                gp.instantiate()
+                gt = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gt, capture_error_mode="thread_local"):
+                    self._launch(seg, events=True)
+            self.plain.append((gp, seg))
+            self.timed.append((gt, seg))
         torch.cuda.synchronize()
-        self.kernel_nodes = sum(f.kernel_nodes for f in frags) if use_graphs else None
+        self.kernel_nodes = n_nodes if use_graphs else None
 
     @staticmethod
-    def _launch(seg):
+    def _launch(seg, events):
         for f in seg:
-            f.ev[0].record()
+            if events:
+                f.ev[0].record()
             for si, (_, fn) in enumerate(f.stages):
                 fn()
-                f.ev[si + 1].record()
+                if events:
+                    f.ev[si + 1].record()
 
-    def run(self):
-        for g, seg in self.segments:
+    def _run(self, graphs, events):
+        for g, seg in graphs:
             if g is not None:
                 g.replay()
             else:
-                self._launch(seg)
+                self._launch(seg, events)
             last = seg[-1]
             if last.exchange is not None:
                 last.exchange()
-                last.ev_end.record()
+                if events:
+                    last.ev_end.record()
+
+    def run(self):
+        """One step as timed: no timing events inside."""
+        self._run(self.plain, events=False)
+
+    def run_instrumented(self):
+        self._run(self.timed, events=True)
+
+    def release(self):
+        self.plain, self.timed = [], []
 
     def breakdown(self):
-        """Per-fragment and per-stage ms of the last completed step."""
+        """Per-fragment and per-stage ms of the last instrumented step."""
         out = {}
         for f in self.frags:
             st = [f.ev[i].elapsed_time(f.ev[i + 1]) for i in range(len(f.stages))]
@@ -645,7 +662,7 @@ def ours_arm(args, rank, local_rank, world):
         if world > 1:
             dist.barrier()  # start every breakdown replay together, so no rank's
             torch.cuda.synchronize()  # exchange absorbs another rank's skew
-        step.run()
+        step.run_instrumented()
         torch.cuda.synchronize()
         for name, (fm, st) in step.breakdown().items():
             frag_ms[name].append(fm)
@@ -706,7 +723,7 @@ def ours_arm(args, rank, local_rank, world):
         line["e2e"] = e2e_measure(frags, args.e2e_steps, world, dev, step_bytes)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(names, args.cpu_seconds)
-    step.segments = []
+    step.release()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -22,6 +22,7 @@
 #include <cub/device/device_radix_sort.cuh>
 
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -314,6 +315,25 @@ emb_bwd_rows_generic(const uint32_t* __restrict__ keys, const uint32_t* __restri
   }
 }
 
+// A second stream per device for the zero sweep, so it runs while the sort
+// and the token kernel run on the caller's stream (joined before returning).
+cudaStream_t side_stream() {
+  static std::mutex mu;
+  static cudaStream_t streams[64] = {};
+  const int d = current_device();
+  if (d < 0 || d >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (streams[d] == nullptr) {
+    cudaStream_t st = nullptr;
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    streams[d] = st;
+  }
+  return streams[d];
+}
+
 struct BwdLayout {
   size_t keys_in, vals_in, keys_out, vals_out, touched, touched_bytes, temp, temp_bytes, total;
 };
@@ -415,18 +435,74 @@ int frag_embedding_bwd(const int64_t* ids, const void* grad, float* G, int64_t T
         ids, Ti, vocab_lo, shard_rows, vocab_total, padding_idx, keys_in, vals_in, touched, status);
     int st = check_launch();
     if (st != FRAG_OK) return st;
-    size_t tb = L.temp_bytes;
-    if (cuda_status(cub::DeviceRadixSort::SortPairs(ws + L.temp, tb, keys_in, keys_out, vals_in,
-                                                    vals_out, Ti, 0, sort_end_bit(shard_rows),
-                                                    s)) != FRAG_OK)
-      return FRAG_ERR_CUDA;
   }
+  auto sort_pairs = [&](cudaStream_t on) -> int {
+    if (Ti == 0) return FRAG_OK;
+    size_t tb = L.temp_bytes;
+    return cuda_status(cub::DeviceRadixSort::SortPairs(ws + L.temp, tb, keys_in, keys_out, vals_in,
+                                                       vals_out, Ti, 0, sort_end_bit(shard_rows), on));
+  };
 
+  int sms = sm_count();
+  if (sms <= 0) sms = 148;
   auto g = static_cast<const uint16_t*>(grad);
   const int64_t quads = D / 4;
   const bool vec = D % 4 == 0 && quads <= 8 * 256 && (Ti == 0 || (reinterpret_cast<uintptr_t>(grad) & 7) == 0) &&
                    aligned16(G);
-  // One wave of CTAs, each owning a contiguous block of rows.
+
+  // Zero sweep + token CTAs: widths that are multiples of 8 up to 4096, rows
+  // 32-byte aligned (256-bit stores) and gradient rows 16-byte aligned.  The
+  // sweep depends only on the bitmap, so it runs on a side stream while the
+  // sort and the token kernel run on `s`; `s` then waits for it.
+  const int64_t units = D / 8;
+  if (D % 8 == 0 && units <= 4 * 128 && (reinterpret_cast<uintptr_t>(G) & 31) == 0 &&
+      (Ti == 0 || aligned16(grad))) {
+    const int Di = static_cast<int>(D);
+    const int64_t zgrid = std::min<int64_t>(static_cast<int64_t>(sms) * 32,
+                                            std::max<int64_t>(1, ceil_div(shard_rows * units, 256)));
+    cudaStream_t zs = (Ti > 0) ? side_stream() : nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+    if (zs && (cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) != cudaSuccess ||
+               cudaEventCreateWithFlags(&join, cudaEventDisableTiming) != cudaSuccess)) {
+      cudaGetLastError();
+      if (fork) cudaEventDestroy(fork);
+      fork = join = nullptr;
+      zs = nullptr;
+    }
+    if (zs) {
+      if (cuda_status(cudaEventRecord(fork, s)) != FRAG_OK ||
+          cuda_status(cudaStreamWaitEvent(zs, fork, 0)) != FRAG_OK)
+        return FRAG_ERR_CUDA;
+    }
+    emb_bwd_zero<<<dim3(static_cast<unsigned>(zgrid)), 256, 0, zs ? zs : s>>>(touched, G, shard_rows, Di);
+    int st = check_launch();
+    if (zs) {
+      // the join is recorded whatever happened above, so the side stream is
+      // always joined back into `s` (a stream capture must not end forked)
+      const int sj = cuda_status(cudaEventRecord(join, zs));
+      if (st == FRAG_OK) st = sj;
+    }
+    if (st == FRAG_OK) st = sort_pairs(s);
+    if (st == FRAG_OK && Ti > 0) {
+      const dim3 tgrid(static_cast<unsigned>(ceil_div(T, kTokPerCta)));
+      if (units <= 128)
+        emb_bwd_tokens<1><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
+      else if (units <= 256)
+        emb_bwd_tokens<2><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
+      else
+        emb_bwd_tokens<4><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
+      st = check_launch();
+    }
+    if (zs) {
+      const int sj = cuda_status(cudaStreamWaitEvent(s, join, 0));
+      if (st == FRAG_OK) st = sj;
+      cudaEventDestroy(fork);
+      cudaEventDestroy(join);
+    }
+    return st;
+  }
+  if (sort_pairs(s) != FRAG_OK) return FRAG_ERR_CUDA;
+  // Fallback row kernels (other widths / alignments): a CTA per block of rows.
   int per_sm = 0;
   cudaError_t oe;
   if (!vec) oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, emb_bwd_rows_generic, 256, 0);
@@ -438,32 +514,10 @@ int frag_embedding_bwd(const int64_t* ids, const void* grad, float* G, int64_t T
     cudaGetLastError();
     per_sm = 4;
   }
-  int sms = sm_count();
-  if (sms <= 0) sms = 148;
   const int64_t target =
       std::max<int64_t>(1, std::min<int64_t>(shard_rows, static_cast<int64_t>(sms) * std::max(per_sm, 1)));
   const int64_t rpb = ceil_div(shard_rows, target);
   const dim3 grid(static_cast<unsigned>(ceil_div(shard_rows, rpb)));
-  // Zero sweep + token CTAs: widths that are multiples of 8 up to 4096, rows
-  // 32-byte aligned (256-bit stores) and gradient rows 16-byte aligned.
-  const int64_t units = D / 8;
-  if (D % 8 == 0 && units <= 4 * 128 && (reinterpret_cast<uintptr_t>(G) & 31) == 0 &&
-      (Ti == 0 || aligned16(grad))) {
-    const int Di = static_cast<int>(D);
-    const int64_t zgrid = std::min<int64_t>(static_cast<int64_t>(sms) * 32,
-                                            std::max<int64_t>(1, ceil_div(shard_rows * units, 256)));
-    emb_bwd_zero<<<dim3(static_cast<unsigned>(zgrid)), 256, 0, s>>>(touched, G, shard_rows, Di);
-    int st2 = check_launch();
-    if (st2 != FRAG_OK || Ti == 0) return st2;
-    const dim3 tgrid(static_cast<unsigned>(ceil_div(T, kTokPerCta)));
-    if (units <= 128)
-      emb_bwd_tokens<1><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
-    else if (units <= 256)
-      emb_bwd_tokens<2><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
-    else
-      emb_bwd_tokens<4><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
-    return check_launch();
-  }
   if (vec) {
     const int Di = static_cast<int>(D);
     if (quads <= 256)
