@@ -52,7 +52,7 @@ DOMINANT = "C4B"  # largest share of the step; its main kernel is the roofline k
 # Fusions beyond the five configurations (SURVEY "next" rows), measured on request:
 #   C2N  embedding gather + RMSNorm fused (C2 ids/table, eps 1e-5)
 #   C3S  RoPE fwd writing q/k in the [B, H, S, D] layout attention reads (C3 shapes)
-NEXT = ["C2N", "C3S"]
+NEXT = ["C2N", "C3S", "C2C", "C2U"]
 
 
 # ------------------------------------------------------------------ helpers
@@ -441,7 +441,53 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
                                                         out_layout="bhsd"), h)
         return f
 
-    builders = {"C2N": mk_c2n, "C3S": mk_c3s, "C0F": mk_c0f, "C1B": lambda: mk_rms_bwd("C1B", C1, False, 3, False),
+    def mk_chain(which):
+        # RMSNorm backward -> residual add -> embedding backward at the shapes
+        # of the reference chain problem (v6/0b493aad68f0: 8192 tokens, width
+        # 4096, 128256-row table, ids uniform in [0, 100), three summed
+        # gradients, rstd recomputed, y returned).  C2C is the fused kernel;
+        # C2U the same chain composed of the unfused calls (d_emb round trip).
+        T, D, V = 8192, 4096, 128256
+        x = cf.randn((1, T, D), device=dev, seed=seed0 + 30)
+        w = cf.randn((D,), device=dev, seed=seed0 + 31)
+        dys = [cf.randn((T, D), device=dev, seed=seed0 + 32 + j) for j in range(3)]
+        dres = cf.randn((1, T, D), device=dev, seed=seed0 + 35)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed0 + 36)
+        ids = torch.randint(0, 100, (1, T), generator=gen, device=dev)
+        Gt = torch.empty(V, D, dtype=torch.float32, device=dev)
+        nb = cf.bytes_rmsnorm_embedding_bwd(T, D, V)
+        name = "norm bwd -> embedding bwd chain [8192,4096] vocab 128256"
+        if which == "C2C":
+            ws = torch.empty(max(16, ops._lib.load().frag_rmsnorm_embedding_bwd_workspace_bytes(T, D, V)),
+                             dtype=torch.uint8, device=dev)
+            f = Frag("C2C", name + " fused", T, nb,
+                     [("rmsnorm_embedding_bwd",
+                       lambda: ops.rmsnorm_embedding_bwd(x, w, ids, dys, V, dres=dres, eps=1e-5,
+                                                         write_y=True, out=Gt, workspace=ws))])
+            f.host = dict(x=x, g0=dys[0], g1=dys[1], g2=dys[2], dres=dres, ids=ids)
+            f.e2e = lambda h: _e2e_call(lambda xs: ops.rmsnorm_embedding_bwd(
+                xs["x"], w, xs["ids"], [xs["g0"], xs["g1"], xs["g2"]], V, dres=xs["dres"], eps=1e-5,
+                write_y=True), h)
+            return f
+        wsb = torch.empty(max(16, ops._lib.load().frag_embedding_bwd_workspace_bytes(T, V)),
+                          dtype=torch.uint8, device=dev)
+        y = torch.empty_like(x)
+        r = torch.empty((1, T), dtype=torch.float32, device=dev)
+
+        def unfused(x, g0, g1, g2, dres, ids, out=None, ws=None, y=None, r=None):
+            y, r = ops.rmsnorm_fwd(x, w, 1e-5, out=y, rstd=r)
+            dy01 = torch.add(g0, g1).view(x.shape)
+            d_emb, dw = ops.rmsnorm_bwd(dy01, x, r, w, dy2=g2.view(x.shape), dres=dres)
+            return ops.embedding_bwd(d_emb, ids, V, out=out, workspace=ws), dw, y
+        f = Frag("C2U", name + " unfused", T, nb,
+                 [("chain_unfused", lambda: unfused(x, *dys, dres, ids, out=Gt, ws=wsb, y=y, r=r))])
+        f.host = dict(x=x, g0=dys[0], g1=dys[1], g2=dys[2], dres=dres, ids=ids)
+        f.e2e = lambda h: _e2e_call(lambda xs: unfused(**xs), h)
+        return f
+
+    builders = {"C2N": mk_c2n, "C3S": mk_c3s, "C2C": lambda: mk_chain("C2C"),
+                "C2U": lambda: mk_chain("C2U"), "C0F": mk_c0f, "C1B": lambda: mk_rms_bwd("C1B", C1, False, 3, False),
                 "C2F": lambda: mk_c2("C2F"), "C2B": lambda: mk_c2("C2B"),
                 "C3F": lambda: mk_c3("C3F"), "C3B": lambda: mk_c3("C3B"),
                 "C4F": mk_c4f, "C4B": lambda: mk_rms_bwd("C4B", C4, True, 23, True)}
@@ -721,7 +767,7 @@ def ours_arm(args, rank, local_rank, world):
     # e2e through the public API with host buffers (every step: H2D inputs, D2H outputs)
     if not args.no_e2e:
         line["e2e"] = e2e_measure(frags, args.e2e_steps, world, dev, step_bytes)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and set(names) <= set(SUITE):
         line["cpu_baseline"] = cpu_baseline(names, args.cpu_seconds)
     step.release()
     if world > 1:

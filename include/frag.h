@@ -218,6 +218,40 @@ FRAG_API int frag_embedding_bwd(const int64_t* ids, const void* grad, float* G,
                        frag_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
+ * RMSNorm backward fused into the token-embedding backward (deterministic).
+ * For every token t (x = the embedding output that entered the norm):
+ *   dy     = bf16(bf16(dy_a + dy_b) + dy_c)     (dy_b, dy_c optional, in order)
+ *   rstd   = the saved rstd[t], or rsqrt(mean(x^2) + eps) when rstd is NULL
+ *   y      = bf16((x * rstd) * w)               (written when y is not NULL)
+ *   dx     = bf16(rstd * (dy*w - xhat * mean(dy*w*xhat))),  xhat = x * rstd
+ *   d_emb  = bf16(dres + dx), or dx without dres (written when d_emb is not NULL)
+ *   G[v,:] = sum of d_emb over the tokens of row v (as frag_embedding_bwd:
+ *            shard-local rows, padding skipped, every row written once, fixed
+ *            order), dw = sum over t of dy * xhat (fp32, fixed order).
+ * d_emb never has to exist in memory.
+ * Replaces _fused_rms_norm -> add -> add -> _fused_rms_norm_backward -> add ->
+ * _to_copy -> embedding_dense_backward -> _to_copy of
+ *   v6/0b493aad68f0/problem.py:21-70 (drop-in v6/0b493aad68f0/optimized_kernel.py:100),
+ *   v5/118d525f44e0/problem.py (drop-in v5/118d525f44e0/optimized_kernel.py:72),
+ *   v4/680e4c57cdc8/problem.py (drop-in v4/680e4c57cdc8/optimized_kernel.py:69),
+ *   and, with the saved rstd, v8/f6251e84e3fa/problem.py:22-57.
+ * x, dy_*, dres, y, d_emb: bf16 [T, D]; w: bf16 [D]; rstd: fp32 [T] or NULL;
+ * ids: int64 [T]; G: fp32 [shard_rows, D]; dw: fp32 [D] and/or dw_bf16: bf16 [D].
+ * workspace: frag_rmsnorm_embedding_bwd_workspace_bytes(T, D, shard_rows).
+ * ------------------------------------------------------------------------- */
+FRAG_API size_t frag_rmsnorm_embedding_bwd_workspace_bytes(int64_t T, int64_t D,
+                                                           int64_t shard_rows);
+FRAG_API int frag_rmsnorm_embedding_bwd(const void* x, const void* w, const float* rstd,
+                                        void* y, const void* dy_a, const void* dy_b,
+                                        const void* dy_c, const void* dres, void* d_emb,
+                                        const int64_t* ids, float* G, float* dw,
+                                        void* dw_bf16, int64_t T, int64_t D,
+                                        int64_t shard_rows, int64_t vocab_lo,
+                                        int64_t vocab_total, int64_t padding_idx, float eps,
+                                        void* workspace, size_t workspace_bytes,
+                                        int32_t* status, frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
  * Rotary position embedding on up to two tensors (q and k) in one launch.
  * Tensor i (i = 0, 1) is bf16 [B, S, H_i, D] addressed by element strides
  * (stride_b, stride_s, stride_h; the last dimension is contiguous), and is

@@ -113,6 +113,15 @@ def bytes_embedding_bwd(T: int, D: int, rows: int) -> int:
     return T * D * BF16 + T * I64 + rows * D * F32
 
 
+def bytes_rmsnorm_embedding_bwd(T: int, D: int, rows: int, n_dy: int = 3, dres: bool = True,
+                                y: bool = True) -> int:
+    # x, the dy terms and dres read; w, ids read; y (recomputed forward) and
+    # the fp32 table gradient and dweight written.  d_emb is not counted: the
+    # fused kernel never stores it.
+    return ((1 + n_dy + (1 if dres else 0) + (1 if y else 0)) * T * D * BF16 + D * BF16 + T * I64
+            + rows * D * F32 + D * F32)
+
+
 def bytes_rope(T: int, Hq: int, Hk: int, D: int) -> int:
     return 2 * T * (Hq + Hk) * D * BF16 + T * I64
 

@@ -170,6 +170,14 @@ __device__ __forceinline__ float block_sum(float v, float (*slots)[32], int pari
   return t;
 }
 
+// Round two fp32 values to the nearest bf16 (ties to even) with one packed
+// conversion and widen them back.
+__device__ __forceinline__ void round_bf16x2(float& a, float& b) {
+  const uint32_t u = pack_bf16x2(a, b);
+  a = bf16lo(u);
+  b = bf16hi(u);
+}
+
 // --------------------------------------------- TMA bulk copies + mbarriers
 //
 // One-dimensional bulk copies (cp.async.bulk) move whole rows from global to

@@ -25,6 +25,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "emb_bwd.cuh"
 
 namespace frag {
 namespace {
@@ -222,6 +223,19 @@ emb_bwd_zero(const uint32_t* __restrict__ touched, float* __restrict__ G, int64_
   }
 }
 
+// Zero sweep for any width and alignment (scalar stores).
+__global__ void __launch_bounds__(256)
+emb_bwd_zero_generic(const uint32_t* __restrict__ touched, float* __restrict__ G, int64_t shard_rows,
+                     int64_t D) {
+  const int64_t total = shard_rows * D;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < total;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = u / D;
+    if (__ldg(touched + (row >> 5)) & (1u << (row & 31))) continue;
+    G[u] = 0.f;
+  }
+}
+
 template <int U>  // 8-float units per thread and row (128 threads)
 __global__ void __launch_bounds__(128)
 emb_bwd_tokens(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, int T,
@@ -334,17 +348,15 @@ cudaStream_t side_stream() {
   return streams[d];
 }
 
-struct BwdLayout {
-  size_t keys_in, vals_in, keys_out, vals_out, touched, touched_bytes, temp, temp_bytes, total;
-};
-
 int sort_end_bit(int64_t shard_rows) {
   int b = 0;
   while (b < 32 && (static_cast<uint64_t>(shard_rows) >> b) != 0) ++b;
   return std::max(b, 1);
 }
 
-bool bwd_layout(int64_t T, int64_t shard_rows, BwdLayout* L) {
+}  // namespace
+
+bool emb_bwd_layout(int64_t T, int64_t shard_rows, EmbBwdLayout* L) {
   size_t temp_bytes = 0;
   const int n = static_cast<int>(std::max<int64_t>(T, 1));
   if (cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, static_cast<const uint32_t*>(nullptr),
@@ -368,7 +380,94 @@ bool bwd_layout(int64_t T, int64_t shard_rows, BwdLayout* L) {
   return true;
 }
 
-}  // namespace
+int emb_bwd_front(const int64_t* ids, int T, int64_t shard_rows, int64_t D, int64_t vocab_lo,
+                  int64_t vocab_total, int64_t padding_idx, float* G, bool zero_sweep,
+                  int zero_ctas_per_sm, bool sort_first, char* ws, const EmbBwdLayout& L,
+                  int32_t* status, cudaStream_t s, EmbBwdFront* f) {
+  auto keys_in = reinterpret_cast<uint32_t*>(ws + L.keys_in);
+  auto vals_in = reinterpret_cast<uint32_t*>(ws + L.vals_in);
+  auto keys_out = reinterpret_cast<uint32_t*>(ws + L.keys_out);
+  auto vals_out = reinterpret_cast<uint32_t*>(ws + L.vals_out);
+  auto touched = reinterpret_cast<uint32_t*>(ws + L.touched);
+  f->keys = keys_out;
+  f->vals = vals_out;
+  f->touched = touched;
+  f->fork = f->join = nullptr;
+
+  if (cuda_status(cudaMemsetAsync(touched, 0, L.touched_bytes, s)) != FRAG_OK) return FRAG_ERR_CUDA;
+  if (T > 0) {
+    emb_bwd_prep<<<dim3(static_cast<unsigned>(ceil_div(T, 256))), 256, 0, s>>>(
+        ids, T, vocab_lo, shard_rows, vocab_total, padding_idx, keys_in, vals_in, touched, status);
+    const int st = check_launch();
+    if (st != FRAG_OK) return st;
+  }
+  auto sort = [&]() -> int {
+    if (T <= 0) return FRAG_OK;
+    size_t tb = L.temp_bytes;
+    return cuda_status(cub::DeviceRadixSort::SortPairs(ws + L.temp, tb, keys_in, keys_out, vals_in,
+                                                       vals_out, T, 0, sort_end_bit(shard_rows), s));
+  };
+  if (sort_first) {
+    const int st = sort();
+    if (st != FRAG_OK) return st;
+  }
+  if (zero_sweep) {
+    int sms = sm_count();
+    if (sms <= 0) sms = 148;
+    // The sweep depends only on the bitmap: with tokens to sort (and the
+    // sort still to come) it runs on a side stream, forked here and joined
+    // by emb_bwd_join; after the sort it runs on `s` itself.
+    cudaStream_t zs = (T > 0 && !sort_first) ? side_stream() : nullptr;
+    if (zs && (cudaEventCreateWithFlags(&f->fork, cudaEventDisableTiming) != cudaSuccess ||
+               cudaEventCreateWithFlags(&f->join, cudaEventDisableTiming) != cudaSuccess)) {
+      cudaGetLastError();
+      if (f->fork) cudaEventDestroy(f->fork);
+      f->fork = f->join = nullptr;
+      zs = nullptr;
+    }
+    if (zs) {
+      const int a = cuda_status(cudaEventRecord(f->fork, s));
+      const int b = (a == FRAG_OK) ? cuda_status(cudaStreamWaitEvent(zs, f->fork, 0)) : a;
+      if (b != FRAG_OK) {
+        cudaEventDestroy(f->fork);
+        cudaEventDestroy(f->join);
+        f->fork = f->join = nullptr;
+        return b;
+      }
+    }
+    cudaStream_t on = zs ? zs : s;
+    const bool vec = D % 8 == 0 && (reinterpret_cast<uintptr_t>(G) & 31) == 0;
+    const int64_t per_thread = vec ? D / 8 : D;
+    const int64_t zgrid = std::min<int64_t>(static_cast<int64_t>(sms) * std::max(zero_ctas_per_sm, 1),
+                                            std::max<int64_t>(1, ceil_div(shard_rows * per_thread, 256)));
+    if (vec) {
+      emb_bwd_zero<<<dim3(static_cast<unsigned>(zgrid)), 256, 0, on>>>(touched, G, shard_rows,
+                                                                       static_cast<int>(D));
+    } else {
+      emb_bwd_zero_generic<<<dim3(static_cast<unsigned>(zgrid)), 256, 0, on>>>(touched, G, shard_rows, D);
+    }
+    int st = check_launch();
+    if (zs) {
+      // recorded whatever happened above, so the join always has an event
+      const int sj = cuda_status(cudaEventRecord(f->join, zs));
+      if (st == FRAG_OK) st = sj;
+    }
+    if (st != FRAG_OK) return st;
+  }
+  return sort_first ? FRAG_OK : sort();
+}
+
+int emb_bwd_join(EmbBwdFront* f, cudaStream_t s, int st) {
+  if (f->join) {
+    const int sj = cuda_status(cudaStreamWaitEvent(s, f->join, 0));
+    if (st == FRAG_OK) st = sj;
+  }
+  if (f->fork) cudaEventDestroy(f->fork);
+  if (f->join) cudaEventDestroy(f->join);
+  f->fork = f->join = nullptr;
+  return st;
+}
+
 }  // namespace frag
 
 using namespace frag;
@@ -403,8 +502,8 @@ int frag_embedding_fwd(const int64_t* ids, const void* table, void* out, int64_t
 
 size_t frag_embedding_bwd_workspace_bytes(int64_t T, int64_t shard_rows) {
   if (T < 0 || shard_rows < 0 || T > 0x7fffffffLL || shard_rows >= 0xffffffffLL) return 0;
-  BwdLayout L;
-  if (!bwd_layout(T, shard_rows, &L)) return 0;
+  EmbBwdLayout L;
+  if (!emb_bwd_layout(T, shard_rows, &L)) return 0;
   return L.total;
 }
 
@@ -417,92 +516,51 @@ int frag_embedding_bwd(const int64_t* ids, const void* grad, float* G, int64_t T
   if (!G || (T > 0 && (!ids || !grad))) return FRAG_ERR_INVALID_ARG;
   if (T > 0x7fffffffLL || shard_rows >= 0xffffffffLL) return FRAG_ERR_SHAPE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  BwdLayout L;
-  if (!bwd_layout(T, shard_rows, &L)) return FRAG_ERR_CUDA;
+  EmbBwdLayout L;
+  if (!emb_bwd_layout(T, shard_rows, &L)) return FRAG_ERR_CUDA;
   if (!workspace || workspace_bytes < L.total) return FRAG_ERR_WORKSPACE;
   if (!aligned16(workspace)) return FRAG_ERR_ALIGN;
   char* ws = static_cast<char*>(workspace);
-  auto keys_in = reinterpret_cast<uint32_t*>(ws + L.keys_in);
-  auto vals_in = reinterpret_cast<uint32_t*>(ws + L.vals_in);
-  auto keys_out = reinterpret_cast<uint32_t*>(ws + L.keys_out);
-  auto vals_out = reinterpret_cast<uint32_t*>(ws + L.vals_out);
-  auto touched = reinterpret_cast<uint32_t*>(ws + L.touched);
   const int Ti = static_cast<int>(T);
-
-  if (cuda_status(cudaMemsetAsync(touched, 0, L.touched_bytes, s)) != FRAG_OK) return FRAG_ERR_CUDA;
-  if (Ti > 0) {
-    emb_bwd_prep<<<dim3(static_cast<unsigned>(ceil_div(T, 256))), 256, 0, s>>>(
-        ids, Ti, vocab_lo, shard_rows, vocab_total, padding_idx, keys_in, vals_in, touched, status);
-    int st = check_launch();
-    if (st != FRAG_OK) return st;
-  }
-  auto sort_pairs = [&](cudaStream_t on) -> int {
-    if (Ti == 0) return FRAG_OK;
-    size_t tb = L.temp_bytes;
-    return cuda_status(cub::DeviceRadixSort::SortPairs(ws + L.temp, tb, keys_in, keys_out, vals_in,
-                                                       vals_out, Ti, 0, sort_end_bit(shard_rows), on));
-  };
-
   int sms = sm_count();
   if (sms <= 0) sms = 148;
   auto g = static_cast<const uint16_t*>(grad);
-  const int64_t quads = D / 4;
-  const bool vec = D % 4 == 0 && quads <= 8 * 256 && (Ti == 0 || (reinterpret_cast<uintptr_t>(grad) & 7) == 0) &&
-                   aligned16(G);
 
   // Zero sweep + token CTAs: widths that are multiples of 8 up to 4096, rows
   // 32-byte aligned (256-bit stores) and gradient rows 16-byte aligned.  The
-  // sweep depends only on the bitmap, so it runs on a side stream while the
-  // sort and the token kernel run on `s`; `s` then waits for it.
+  // sweep runs on the side stream while the sort and the token kernel run on
+  // `s`.
   const int64_t units = D / 8;
   if (D % 8 == 0 && units <= 4 * 128 && (reinterpret_cast<uintptr_t>(G) & 31) == 0 &&
       (Ti == 0 || aligned16(grad))) {
-    const int Di = static_cast<int>(D);
-    const int64_t zgrid = std::min<int64_t>(static_cast<int64_t>(sms) * 32,
-                                            std::max<int64_t>(1, ceil_div(shard_rows * units, 256)));
-    cudaStream_t zs = (Ti > 0) ? side_stream() : nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
-    if (zs && (cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) != cudaSuccess ||
-               cudaEventCreateWithFlags(&join, cudaEventDisableTiming) != cudaSuccess)) {
-      cudaGetLastError();
-      if (fork) cudaEventDestroy(fork);
-      fork = join = nullptr;
-      zs = nullptr;
-    }
-    if (zs) {
-      if (cuda_status(cudaEventRecord(fork, s)) != FRAG_OK ||
-          cuda_status(cudaStreamWaitEvent(zs, fork, 0)) != FRAG_OK)
-        return FRAG_ERR_CUDA;
-    }
-    emb_bwd_zero<<<dim3(static_cast<unsigned>(zgrid)), 256, 0, zs ? zs : s>>>(touched, G, shard_rows, Di);
-    int st = check_launch();
-    if (zs) {
-      // the join is recorded whatever happened above, so the side stream is
-      // always joined back into `s` (a stream capture must not end forked)
-      const int sj = cuda_status(cudaEventRecord(join, zs));
-      if (st == FRAG_OK) st = sj;
-    }
-    if (st == FRAG_OK) st = sort_pairs(s);
+    EmbBwdFront f;
+    int st = emb_bwd_front(ids, Ti, shard_rows, D, vocab_lo, vocab_total, padding_idx, G,
+                           /*zero_sweep=*/true, /*zero_ctas_per_sm=*/32, /*sort_first=*/false, ws,
+                           L, status, s, &f);
     if (st == FRAG_OK && Ti > 0) {
+      const int Di = static_cast<int>(D);
       const dim3 tgrid(static_cast<unsigned>(ceil_div(T, kTokPerCta)));
       if (units <= 128)
-        emb_bwd_tokens<1><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
+        emb_bwd_tokens<1><<<tgrid, 128, 0, s>>>(f.keys, f.vals, Ti, g, G, shard_rows, Di);
       else if (units <= 256)
-        emb_bwd_tokens<2><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
+        emb_bwd_tokens<2><<<tgrid, 128, 0, s>>>(f.keys, f.vals, Ti, g, G, shard_rows, Di);
       else
-        emb_bwd_tokens<4><<<tgrid, 128, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di);
+        emb_bwd_tokens<4><<<tgrid, 128, 0, s>>>(f.keys, f.vals, Ti, g, G, shard_rows, Di);
       st = check_launch();
     }
-    if (zs) {
-      const int sj = cuda_status(cudaStreamWaitEvent(s, join, 0));
-      if (st == FRAG_OK) st = sj;
-      cudaEventDestroy(fork);
-      cudaEventDestroy(join);
-    }
-    return st;
+    return emb_bwd_join(&f, s, st);
   }
-  if (sort_pairs(s) != FRAG_OK) return FRAG_ERR_CUDA;
-  // Fallback row kernels (other widths / alignments): a CTA per block of rows.
+
+  // Fallback row kernels (other widths / alignments): a CTA per block of
+  // rows writes every row of its block, so no zero sweep.
+  EmbBwdFront f;
+  int st = emb_bwd_front(ids, Ti, shard_rows, D, vocab_lo, vocab_total, padding_idx, G,
+                         /*zero_sweep=*/false, 0, /*sort_first=*/true, ws, L, status, s, &f);
+  st = emb_bwd_join(&f, s, st);
+  if (st != FRAG_OK) return st;
+  const int64_t quads = D / 4;
+  const bool vec = D % 4 == 0 && quads <= 8 * 256 && (Ti == 0 || (reinterpret_cast<uintptr_t>(grad) & 7) == 0) &&
+                   aligned16(G);
   int per_sm = 0;
   cudaError_t oe;
   if (!vec) oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, emb_bwd_rows_generic, 256, 0);
@@ -521,15 +579,15 @@ int frag_embedding_bwd(const int64_t* ids, const void* grad, float* G, int64_t T
   if (vec) {
     const int Di = static_cast<int>(D);
     if (quads <= 256)
-      emb_bwd_rows_vec<1><<<grid, 256, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di, rpb);
+      emb_bwd_rows_vec<1><<<grid, 256, 0, s>>>(f.keys, f.vals, Ti, g, G, shard_rows, Di, rpb);
     else if (quads <= 512)
-      emb_bwd_rows_vec<2><<<grid, 256, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di, rpb);
+      emb_bwd_rows_vec<2><<<grid, 256, 0, s>>>(f.keys, f.vals, Ti, g, G, shard_rows, Di, rpb);
     else if (quads <= 1024)
-      emb_bwd_rows_vec<4><<<grid, 256, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di, rpb);
+      emb_bwd_rows_vec<4><<<grid, 256, 0, s>>>(f.keys, f.vals, Ti, g, G, shard_rows, Di, rpb);
     else
-      emb_bwd_rows_vec<8><<<grid, 256, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, Di, rpb);
+      emb_bwd_rows_vec<8><<<grid, 256, 0, s>>>(f.keys, f.vals, Ti, g, G, shard_rows, Di, rpb);
   } else {
-    emb_bwd_rows_generic<<<grid, 256, 0, s>>>(keys_out, vals_out, Ti, g, G, shard_rows, D, rpb);
+    emb_bwd_rows_generic<<<grid, 256, 0, s>>>(f.keys, f.vals, Ti, g, G, shard_rows, D, rpb);
   }
   return check_launch();
 }

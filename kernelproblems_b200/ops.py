@@ -32,6 +32,7 @@ __all__ = [
     "embedding_fwd",
     "embedding_rmsnorm_fwd",
     "embedding_bwd",
+    "rmsnorm_embedding_bwd",
     "rope",
     "check_status",
     "reset_status",
@@ -333,6 +334,79 @@ def embedding_bwd(grad: torch.Tensor, ids: torch.Tensor, num_rows: int, *, vocab
     if _SYNC_CHECK:
         check_status(grad.device)
     return G
+
+
+def rmsnorm_embedding_bwd(x: torch.Tensor, weight: torch.Tensor, ids: torch.Tensor,
+                          dy: torch.Tensor | tuple | list, num_rows: int, *,
+                          rstd: torch.Tensor | None = None, dres: torch.Tensor | None = None,
+                          eps: float = 1e-5, write_y: bool = False, return_d_emb: bool = False,
+                          dw_dtype: torch.dtype = torch.float32, vocab_lo: int = 0,
+                          vocab_total: int | None = None, padding_idx: int = -1,
+                          out: torch.Tensor | None = None,
+                          workspace: torch.Tensor | None = None):
+    """RMSNorm backward fused into the table-gradient scatter of its input
+    gradient (the first attention_norm after the token embedding).
+
+    x      the embedding output that entered the norm, bf16 [..., D]
+    dy     one bf16 gradient, or a sequence of up to three summed in order in
+           bf16 (bf16(bf16(a + b) + c), as the reference graph adds them)
+    rstd   saved rstd (fp32, one per token) or None to recompute it with eps
+    dres   optional residual gradient added (bf16) to the norm's dx
+    Returns (G fp32 [num_rows, D], dw [D] (fp32 or bf16), y or None, d_emb or None):
+    y is the recomputed forward bf16(x * rstd * w) (write_y), d_emb the
+    gradient the scatter consumed (return_d_emb; otherwise never stored)."""
+    terms = list(dy) if isinstance(dy, (tuple, list)) else [dy]
+    if not 1 <= len(terms) <= 3:
+        raise ValueError("dy must be one tensor or a sequence of one to three tensors")
+    _need(x, "x", torch.bfloat16)
+    dev = x.device
+    _need(weight, "weight", torch.bfloat16, dev)
+    _need(ids, "ids", torch.int64, dev)
+    D = weight.numel()
+    T = _rows(x, D, "x")
+    if ids.numel() != T:
+        raise ValueError(f"ids has {ids.numel()} elements, x has {T} rows")
+    for j, t in enumerate(terms):
+        _need(t, f"dy[{j}]", torch.bfloat16, dev)
+        if t.numel() != x.numel():
+            raise ValueError(f"dy[{j}] {tuple(t.shape)} does not match x {tuple(x.shape)}")
+        _rows(t, D, f"dy[{j}]")
+    if dres is not None:
+        _need(dres, "dres", torch.bfloat16, dev)
+        if dres.numel() != x.numel():
+            raise ValueError(f"dres {tuple(dres.shape)} does not match x {tuple(x.shape)}")
+        _rows(dres, D, "dres")
+    if rstd is not None:
+        _need(rstd, "rstd", torch.float32, dev)
+        if rstd.numel() != T or not rstd.is_contiguous():
+            raise ValueError(f"rstd must be contiguous with {T} elements")
+    if dw_dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("dw_dtype must be float32 or bfloat16")
+    ids_c = ids.contiguous()
+    total = int(num_rows) if vocab_total is None else int(vocab_total)
+    G = torch.empty(num_rows, D, dtype=torch.float32, device=dev) if out is None else out
+    dw = torch.empty(D, dtype=dw_dtype, device=dev)
+    y = torch.empty_like(x) if write_y else None
+    d_emb = torch.empty_like(x) if return_d_emb else None
+    a, b, c = (terms + [None, None])[:3]
+    wc = weight.contiguous()
+    with _on_device(dev):
+        lib = _lib.load()
+        need = int(lib.frag_rmsnorm_embedding_bwd_workspace_bytes(T, D, num_rows))
+        if need == 0 and D > 0:
+            raise FragError("frag_rmsnorm_embedding_bwd_workspace_bytes", 2, "unsupported sizes")
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+        st = _status_word(dev)
+        _lib.call("frag_rmsnorm_embedding_bwd", _ptr(x), _ptr(wc), _ptr(rstd), _ptr(y),
+                  _ptr(a), _ptr(b), _ptr(c), _ptr(dres), _ptr(d_emb), _ptr(ids_c), _ptr(G),
+                  _ptr(dw) if dw_dtype == torch.float32 else None,
+                  _ptr(dw) if dw_dtype == torch.bfloat16 else None,
+                  T, D, int(num_rows), int(vocab_lo), total, int(padding_idx), float(eps),
+                  _ptr(workspace), workspace.numel(), _ptr(st), _stream(dev))
+    if _SYNC_CHECK:
+        check_status(dev)
+    return G, dw, y, d_emb
 
 
 # ------------------------------------------------------------------- RoPE

@@ -17,8 +17,10 @@ modified; outputs are new tensors on the inputs' device.
 
 Problems whose graphs are outside the library's ops are not registered:
 v7/0f38bc55457c returns q in fp32, v7/ed20955ec34b sums three gradients, and
-v8/43f0c930291e, v8/f6251e84e3fa, v8/7e38211c7f1c are broken in the
-reference itself (their inputs do not match their graphs).
+v8/43f0c930291e, v8/7e38211c7f1c are broken in the reference itself (their
+inputs do not match their graphs).  v8/f6251e84e3fa is broken the same way
+(its first input should be the (y, rstd) pair of a _fused_rms_norm); its
+drop-in is registered and works when given that pair.
 """
 from __future__ import annotations
 
@@ -239,7 +241,54 @@ def rope_sdpa_6b92d6e665ab(arg586_1, arg582_1, mm_217, mm_218):
     return (q.transpose(1, 2), k.transpose(1, 2), q2.transpose(1, 2), k2.transpose(1, 2))
 
 
+# ------------------------------------------- RMSNorm bwd -> embedding bwd
+
+
+def _norm_emb_chain(w, embedding, mm_670, mm_672, mm_674, add_220, ids, rstd=None, write_y=True):
+    x = embedding.contiguous()
+    N = w.numel()
+    dys = [m.contiguous() for m in (mm_670, mm_672, mm_674)]
+    G, dw, y, _ = ops.rmsnorm_embedding_bwd(x, w, ids, dys, VOCAB, rstd=rstd,
+                                            dres=add_220.contiguous(), eps=1e-5, write_y=write_y)
+    return G, dw, (y.view(-1, N) if y is not None else None)
+
+
+def norm_emb_bwd_0b493aad68f0(embedding, _unsafe_view_432, mm_670, mm_672, mm_674, add_220, arg583_1):
+    """v6/0b493aad68f0/optimized_kernel.py:100: _fused_rms_norm of the
+    embedding output (rstd recomputed in the fused kernel), dy = mm_670 +
+    mm_672 + mm_674 (bf16), d_emb = add_220 + dx, scattered into the fp32
+    table gradient without storing d_emb -> (y, y, y [M,N] views, dweight
+    fp32 [4096], table gradient fp32 [128256, 4096])."""
+    G, dw, y = _norm_emb_chain(_unsafe_view_432, embedding, mm_670, mm_672, mm_674, add_220, arg583_1)
+    return (y, y, y, dw, G)
+
+
+def norm_emb_bwd_118d525f44e0(getitem_791, embedding, mm_670, mm_672, mm_674, add_220, arg583_1):
+    """v5/118d525f44e0/optimized_kernel.py:72 and v4/680e4c57cdc8/optimized_kernel.py:69:
+    as 0b493aad68f0 with the weight gathered from the [8, 512] FSDP shard view."""
+    G, dw, y = _norm_emb_chain(_fsdp_weight(getitem_791), embedding, mm_670, mm_672, mm_674, add_220,
+                               arg583_1)
+    return (y, y, y, dw, G)
+
+
+def norm_emb_bwd_f6251e84e3fa(_fused_rms_norm_recomputed, mm_670, mm_672, mm_674, embedding,
+                              _unsafe_view_432, add_220, arg583_1):
+    """v8/f6251e84e3fa/problem.py:22-57: the saved rstd is
+    _fused_rms_norm_recomputed[1] (fp32 [1, S, 1]) -> (dweight fp32, table
+    gradient fp32).  The reference's own get_inputs passes a 0-d tensor here,
+    so indexing it raises IndexError, as the reference Model does."""
+    rstd = _fused_rms_norm_recomputed[1]
+    x = embedding.contiguous()
+    G, dw, _ = _norm_emb_chain(_unsafe_view_432, x, mm_670, mm_672, mm_674, add_220, arg583_1,
+                               rstd=rstd.contiguous().view(x.shape[:-1]), write_y=False)
+    return (dw, G)
+
+
 PROBLEMS: dict[str, Callable] = {
+    "v6/0b493aad68f0": norm_emb_bwd_0b493aad68f0,
+    "v5/118d525f44e0": norm_emb_bwd_118d525f44e0,
+    "v4/680e4c57cdc8": norm_emb_bwd_118d525f44e0,
+    "v8/f6251e84e3fa": norm_emb_bwd_f6251e84e3fa,
     "v8/12545c1e9b06": emb_rms_12545c1e9b06,
     "v4/6b92d6e665ab": rope_sdpa_6b92d6e665ab,
     "v8/f4e9e58fef73": rms_fwd_f4e9e58fef73,

@@ -137,6 +137,25 @@ def embedding_bwd_f64(grad: torch.Tensor, ids: torch.Tensor, num_weights: int,
     return out
 
 
+def rmsnorm_embedding_bwd(x: torch.Tensor, w: torch.Tensor, dys, rstd: torch.Tensor,
+                          dres: torch.Tensor | None, ids: torch.Tensor, num_weights: int,
+                          padding_idx: int = -1):
+    """add -> add -> _fused_rms_norm_backward -> add -> _to_copy ->
+    embedding_dense_backward -> _to_copy (v6/0b493aad68f0/problem.py:45-70,
+    v8/f6251e84e3fa/problem.py:31-56):
+      dy    = bf16 left-fold sum of dys (one aten.add per extra term)
+      dx,dw = rmsnorm_bwd(dy, x, rstd, w)       (bf16)
+      d_emb = bf16(dres + dx)                   (when dres is given)
+    Returns (dw fp32 of the bf16 dw, G fp32 of the bf16 embedding gradient, d_emb, dy)."""
+    dy = dys[0]
+    for t in dys[1:]:
+        dy = aten.add.Tensor(dy, t)
+    dx, dw = rmsnorm_bwd(dy, x, rstd, w)
+    d_emb = aten.add.Tensor(dres, dx) if dres is not None else dx
+    G = embedding_bwd(d_emb, ids, num_weights, padding_idx)
+    return aten._to_copy.default(dw, dtype=torch.float32), G, d_emb, dy
+
+
 # --------------------------------------------------------------------- RoPE
 
 def precompute_freqs_cis(dim: int, end: int, theta: float) -> torch.Tensor:

@@ -170,7 +170,42 @@ def rope_sdpa_6b92d6e665ab(pos, freqs, mm_217, mm_218):
     return (q.transpose(1, 2), k.transpose(1, 2), q2.transpose(1, 2), k2.transpose(1, 2))
 
 
+def _norm_emb_chain(w, embedding, mm_670, mm_672, mm_674, add_220, ids):
+    y, rstd = F.rmsnorm_fwd(embedding, w, 1e-5)
+    y2 = y.view(8192, 4096)
+    v = [aten.view.default(m, [1, 8192, 4096]) for m in (mm_670, mm_672, mm_674)]
+    dw, G, _, _ = F.rmsnorm_embedding_bwd(embedding, w, v, rstd, add_220, ids, 128256)
+    return (y2, y2, y2, dw, G)
+
+
+def norm_emb_bwd_0b493aad68f0(embedding, w, mm_670, mm_672, mm_674, add_220, ids):
+    """v6/0b493aad68f0/problem.py:21-71: _fused_rms_norm of the embedding
+    output (three [M,N] views of y), then the three-gradient backward chain
+    into the table gradient."""
+    return _norm_emb_chain(w, embedding, mm_670, mm_672, mm_674, add_220, ids)
+
+
+def norm_emb_bwd_118d525f44e0(getitem_791, embedding, mm_670, mm_672, mm_674, add_220, ids):
+    """v5/118d525f44e0/problem.py (and v4/680e4c57cdc8): the weight comes from
+    the [8, 512] FSDP shard view (clone -> _unsafe_view [4096])."""
+    w = aten._unsafe_view.default(aten.clone.default(getitem_791, memory_format=torch.contiguous_format), [4096])
+    return _norm_emb_chain(w, embedding, mm_670, mm_672, mm_674, add_220, ids)
+
+
+def norm_emb_bwd_f6251e84e3fa(recomputed, mm_670, mm_672, mm_674, embedding, w, add_220, ids):
+    """v8/f6251e84e3fa/problem.py:22-57: the saved rstd is recomputed[1]; only
+    (dweight fp32, table gradient fp32) are returned."""
+    rstd = recomputed[1]
+    v = [aten.view.default(m, [1, 8192, 4096]) for m in (mm_670, mm_672, mm_674)]
+    dw, G, _, _ = F.rmsnorm_embedding_bwd(embedding, w, v, rstd, add_220, ids, 128256)
+    return (dw, G)
+
+
 ORACLES = {
+    "v6/0b493aad68f0": norm_emb_bwd_0b493aad68f0,
+    "v5/118d525f44e0": norm_emb_bwd_118d525f44e0,
+    "v4/680e4c57cdc8": norm_emb_bwd_118d525f44e0,
+    "v8/f6251e84e3fa": norm_emb_bwd_f6251e84e3fa,
     "v8/12545c1e9b06": emb_rms_12545c1e9b06,
     "v4/6b92d6e665ab": rope_sdpa_6b92d6e665ab,
     "v8/f4e9e58fef73": rms_fwd_f4e9e58fef73,

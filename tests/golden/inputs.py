@@ -45,5 +45,17 @@ def make_input(spec: dict, device="cpu") -> torch.Tensor:
     return base.as_strided(tuple(v["shape"]), tuple(v["stride"]), int(v["offset"]))
 
 
-def make_inputs(specs: list[dict], device="cpu") -> list[torch.Tensor]:
-    return [make_input(s, device) for s in specs]
+# Inputs computed from other inputs of the same problem (see make_golden.py's
+# INPUT_FIXUPS): "fused_rms_norm" is the (y, rstd) pair that
+# aten._fused_rms_norm(inputs[x], [N], inputs[w], eps) returns on the CPU.
+DERIVED = ("fused_rms_norm",)
+
+
+def make_inputs(specs: list[dict], device="cpu") -> list:
+    out = [None if s["kind"] in DERIVED else make_input(s, device) for s in specs]
+    for i, s in enumerate(specs):
+        if s["kind"] == "fused_rms_norm":
+            x, w = out[s["x"]].cpu(), out[s["w"]].cpu()
+            y, rstd = torch.ops.aten._fused_rms_norm.default(x, [w.numel()], w, float(s["eps"]))
+            out[i] = (y.to(device), rstd.to(device))
+    return out

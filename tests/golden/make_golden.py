@@ -30,10 +30,21 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent.parent))
 sys.path.insert(0, str(HERE))
 
-from inputs import base_tensor  # noqa: E402
+from inputs import base_tensor, make_inputs  # noqa: E402
 from kernelproblems_b200.problems import PROBLEMS  # noqa: E402
 
 SEED_BASE = 20260
+
+# Problems whose reference get_inputs() does not match their own graph, with
+# the input rebuilt from the problem's other inputs (tests/golden/inputs.py).
+# v8/f6251e84e3fa: get_inputs passes torch.randn([]) as
+# _fused_rms_norm_recomputed, which the graph indexes [1] (problem.py:22,61),
+# so the reference FAILs with "index 1 is out of bounds" (benchmark.json).
+# The graph wants the (y, rstd) pair of _fused_rms_norm over its own
+# `embedding` (input 4) and weight (input 5) at eps 1e-5.
+INPUT_FIXUPS = {
+    "v8/f6251e84e3fa": {0: {"kind": "fused_rms_norm", "x": 4, "w": 5, "eps": 1e-5}},
+}
 
 
 def sha256(t: torch.Tensor) -> str:
@@ -130,7 +141,10 @@ def main(argv=None):
         mod = load_problem(ref, key)
         with SeededInputs(SEED_BASE + 100 * i) as rec:
             inputs = mod.get_inputs()
-        specs = [rec.spec_for(t) for t in inputs]
+        fix = INPUT_FIXUPS.get(key, {})
+        specs = [fix[j] if j in fix else rec.spec_for(t) for j, t in enumerate(inputs)]
+        if fix:
+            inputs = make_inputs(specs)
         with torch.no_grad():
             outs = mod.Model()(*inputs)
         outs = outs if isinstance(outs, (tuple, list)) else (outs,)

@@ -77,3 +77,13 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.undo()
     _lib._lib = None
     _lib.load()
+
+
+def test_broken_reference_input_fails_like_the_reference():
+    """v8/f6251e84e3fa's own get_inputs passes a 0-d tensor where the graph
+    indexes [1] of the (y, rstd) pair; the reference Model raises IndexError
+    there, and so does the drop-in (before touching the GPU)."""
+    import torch
+    from kernelproblems_b200.problems import PROBLEMS
+    with pytest.raises(IndexError):
+        PROBLEMS["v8/f6251e84e3fa"](torch.randn([]), *[None] * 7)

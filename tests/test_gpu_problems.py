@@ -31,6 +31,25 @@ FIXTURES = sorted(GOLDEN.glob("v*_*.pt"))
 EXACT = {"v7/1e49beb8a123", "v6/1e49beb8a123", "v5/1e49beb8a123", "v4/1e49beb8a123"}
 RMS_BWD = {"v7/45990c83cfd6", "v7/7f544ceb2120", "v8/d8f596b3df34"}
 EMB_BWD = {"v7/a12a160cb11b"}
+# norm -> embedding backward chain: output index of (dweight, table gradient)
+CHAIN = {"v6/0b493aad68f0": (3, 4), "v5/118d525f44e0": (3, 4), "v4/680e4c57cdc8": (3, 4),
+         "v8/f6251e84e3fa": (0, 1)}
+
+
+def _chain_f64(key, cpu_in):
+    """float64 dweight and table gradient of the norm -> embedding backward
+    chain, from the oracle's bf16 dy and d_emb."""
+    if key == "v6/0b493aad68f0":
+        emb, w, mm_670, mm_672, mm_674, add_220, ids = cpu_in
+    elif key == "v8/f6251e84e3fa":
+        rec, mm_670, mm_672, mm_674, emb, w, add_220, ids = cpu_in
+    else:
+        g791, emb, mm_670, mm_672, mm_674, add_220, ids = cpu_in
+        w = g791.contiguous().view(-1)
+    rstd = rec[1] if key == "v8/f6251e84e3fa" else F.rmsnorm_fwd(emb, w, 1e-5)[1]
+    v = [m.view(emb.shape) for m in (mm_670, mm_672, mm_674)]
+    _, _, d_emb, dy = F.rmsnorm_embedding_bwd(emb, w, v, rstd, add_220, ids, 128256)
+    return F.rmsnorm_dw_f64(dy, emb, rstd), F.embedding_bwd_f64(d_emb, ids, 128256), ids
 
 
 def _check_structure(outs, fx):
@@ -83,6 +102,25 @@ def test_problem_drop_in(fixture):
             assert_f32_close(oc, f64, "table gradient vs float64", atol=(1e-4 * cnt.sqrt()).unsqueeze(1))
             untouched = cnt == 0
             assert torch.count_nonzero(oc[untouched]) == 0
+        elif key in CHAIN and i == CHAIN[key][0]:
+            dw64, _, _ = _chain_f64(key, cpu_in)
+            assert_bf16_close(oc, e, "dweight vs the reference graph", atol=5e-2)
+            assert_f32_close(oc, dw64, "dweight vs float64", atol=1e-3)
+        elif key in CHAIN and i == CHAIN[key][1]:
+            _, g64, ids = _chain_f64(key, cpu_in)
+            cnt = torch.bincount(ids.reshape(-1), minlength=128256)
+            # d_emb is a bf16 tensor in the graph: a rare one-ulp difference in
+            # it (from a different fp32 summation order of the row reduction)
+            # moves a table row by up to one bf16 ulp of |d_emb| (~0.06), the
+            # reference harness's "reduction" tier (atol 0.125)
+            assert_f32_close(oc, g64, "table gradient vs float64", atol=0.125)
+            assert torch.count_nonzero(oc[cnt == 0]) == 0
+            # No golden-row check here: the reference's CPU run accumulates
+            # embedding_dense_backward in bf16 (torch 2.11's CPU kernel), so
+            # with ~80 tokens per id its rows drift from the exact sum by
+            # units; the CUDA aten kernel, like this one, sums in fp32.  The
+            # oracle reproduces that CPU run bit for bit (test_oracle_golden),
+            # and the float64 check above is the accuracy bar.
         elif key in RMS_BWD and i == 1:
             f64, _ = _dw_f64(key, cpu_in)
             assert_bf16_close(oc.float(), e.float(), "dweight vs the reference graph", atol=5e-2)
