@@ -125,6 +125,16 @@ FRAG_API int frag_rmsnorm_bwd(const void* dy, const void* dy2, const void* x,
                      int64_t N, float eps, void* workspace,
                      size_t workspace_bytes, frag_stream_t stream);
 
+/* As frag_rmsnorm_bwd with a third gradient term: dy = bf16(bf16(dy + dy2) +
+ * dy3) (dy3 requires dy2; NULL gives frag_rmsnorm_bwd).  Same workspace.
+ * Replaces add -> add -> _fused_rms_norm_backward -> add -> _to_copy of
+ *   v7/ed20955ec34b/problem.py:19-44 (drop-in v7/ed20955ec34b/optimized_kernel.py:118). */
+FRAG_API int frag_rmsnorm_bwd3(const void* dy, const void* dy2, const void* dy3, const void* x,
+                               const float* rstd, const void* w, const void* dres,
+                               void* dx_out, float* dw, void* dw_bf16, int64_t M, int64_t N,
+                               float eps, void* workspace, size_t workspace_bytes,
+                               frag_stream_t stream);
+
 /* Row-block count G of frag_rmsnorm_bwd for 16-byte aligned operands.  After
  * a frag_rmsnorm_bwd call the first G*N floats of its workspace hold the
  * per-block dweight partials [G, N] (whether or not dw was requested), which

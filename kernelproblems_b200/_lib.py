@@ -77,6 +77,8 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "frag_rmsnorm_bwd_noalloc": (
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
+    "frag_rmsnorm_bwd3": (
+        _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp, _sz, _vp]),
     "frag_rmsnorm_bwd_num_blocks": (_i64, [_i64, _i64]),
     "frag_dw_reduce": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "frag_embedding_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),

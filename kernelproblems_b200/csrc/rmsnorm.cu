@@ -284,6 +284,7 @@ int launch_fwd(const void* res, const void* x, const void* w, void* h, void* y,
 struct BwdIn {
   const uint16_t* dy;
   const uint16_t* dy2;
+  const uint16_t* dy3;  // third gradient term (only with dy2), or nullptr
   const uint16_t* x;
   const float* rstd;
   const uint16_t* w;
@@ -301,7 +302,8 @@ struct BwdIn {
 template <int VPT, bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
 __device__ __forceinline__ void bwd_load_row(const BwdIn& p, int64_t row, int N, int chunks,
                                              uint4 (&dy)[VPT], uint4 (&xx)[VPT],
-                                             uint4 (&dy2)[VPT], uint4 (&dr)[VPT], float& rr) {
+                                             uint4 (&dy2)[VPT], uint4 (&dy3)[VPT],
+                                             uint4 (&dr)[VPT], float& rr) {
   const size_t base = static_cast<size_t>(row) * N;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
@@ -310,10 +312,11 @@ __device__ __forceinline__ void bwd_load_row(const BwdIn& p, int64_t row, int N,
       dy[k] = ld_stream(p.dy + base + c * 8);
       xx[k] = ld_stream(p.x + base + c * 8);
       if (HAS_DY2) dy2[k] = ld_stream(p.dy2 + base + c * 8);
+      if (HAS_DY2) dy3[k] = p.dy3 ? ld_stream(p.dy3 + base + c * 8) : make_uint4(0, 0, 0, 0);
       if (HAS_DRES) dr[k] = ld_stream(p.dres + base + c * 8);
     } else {
       dy[k] = xx[k] = make_uint4(0, 0, 0, 0);
-      if (HAS_DY2) dy2[k] = make_uint4(0, 0, 0, 0);
+      if (HAS_DY2) dy2[k] = dy3[k] = make_uint4(0, 0, 0, 0);
       if (HAS_DRES) dr[k] = make_uint4(0, 0, 0, 0);
     }
   }
@@ -335,14 +338,15 @@ rmsnorm_bwd_vec(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[k][i] = 0.f;
 
-  uint4 cdy[VPT], cx[VPT], cdy2[VPT], cdr[VPT];
+  uint4 cdy[VPT], cx[VPT], cdy2[VPT], cdy3[VPT], cdr[VPT];
   float cr = 0.f;
-  if (r0 < r1) bwd_load_row<VPT, HAS_DY2, HAS_DRES, RECOMPUTE>(p, r0, N, chunks, cdy, cx, cdy2, cdr, cr);
+  if (r0 < r1) bwd_load_row<VPT, HAS_DY2, HAS_DRES, RECOMPUTE>(p, r0, N, chunks, cdy, cx, cdy2, cdy3, cdr, cr);
   int parity = 0;
   for (int64_t row = r0; row < r1; ++row) {
-    uint4 ndy[VPT], nx[VPT], ndy2[VPT], ndr[VPT];
+    uint4 ndy[VPT], nx[VPT], ndy2[VPT], ndy3[VPT], ndr[VPT];
     float nr = 0.f;
-    if (row + 1 < r1) bwd_load_row<VPT, HAS_DY2, HAS_DRES, RECOMPUTE>(p, row + 1, N, chunks, ndy, nx, ndy2, ndr, nr);
+    if (row + 1 < r1)
+      bwd_load_row<VPT, HAS_DY2, HAS_DRES, RECOMPUTE>(p, row + 1, N, chunks, ndy, nx, ndy2, ndy3, ndr, nr);
 
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
@@ -352,13 +356,20 @@ rmsnorm_bwd_vec(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block) {
       float g[8], xf[8], wf[8];
       unpack8(cdy[k], g);
       if (HAS_DY2) {
-        // The summed gradient is a bf16 tensor in the reference graph.
+        // Each partial sum of the gradients is a bf16 tensor in the graph.
         float g2[8];
         unpack8(cdy2[k], g2);
 #pragma unroll
         for (int i = 0; i < 8; ++i) g[i] = g[i] + g2[i];
         cdy[k] = pack8(g);
         unpack8(cdy[k], g);
+        if (p.dy3) {
+          unpack8(cdy3[k], g2);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) g[i] = g[i] + g2[i];
+          cdy[k] = pack8(g);
+          unpack8(cdy[k], g);
+        }
       }
       unpack8(cx[k], xf);
       unpack8(wv, wf);
@@ -397,6 +408,7 @@ rmsnorm_bwd_vec(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block) {
       cdy[k] = ndy[k];
       cx[k] = nx[k];
       if (HAS_DY2) cdy2[k] = ndy2[k];
+      if (HAS_DY2) cdy3[k] = ndy3[k];
       if (HAS_DRES) cdr[k] = ndr[k];
     }
     cr = nr;
@@ -437,9 +449,10 @@ rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, in
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ float2 slots[2][32];
   __shared__ int s_abort;
-  constexpr int NIN = 2 + (HAS_DY2 ? 1 : 0) + (HAS_DRES ? 1 : 0);
+  const bool has3 = HAS_DY2 && p.dy3 != nullptr;
+  const int nin = 2 + (HAS_DY2 ? 1 : 0) + (has3 ? 1 : 0) + (HAS_DRES ? 1 : 0);
   const int row_bytes = N * 2;
-  const int stage_bytes = NIN * row_bytes;
+  const int stage_bytes = nin * row_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * stage_bytes);
   const int chunks = N >> 3;
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
@@ -463,6 +476,7 @@ rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, in
     bulk_g2s(st + row_bytes, p.x + off, row_bytes, bar);
     int slot = 2;
     if (HAS_DY2) bulk_g2s(st + (slot++) * row_bytes, p.dy2 + off, row_bytes, bar);
+    if (has3) bulk_g2s(st + (slot++) * row_bytes, p.dy3 + off, row_bytes, bar);
     if (HAS_DRES) bulk_g2s(st + slot * row_bytes, p.dres + off, row_bytes, bar);
     issued = i + 1;
   };
@@ -493,16 +507,23 @@ rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, in
         gdy[k] = *reinterpret_cast<const uint4*>(st + c * 16);
         gx[k] = *reinterpret_cast<const uint4*>(st + row_bytes + c * 16);
         if (HAS_DY2) {
-          // The summed gradient is a bf16 tensor in the reference graph.
+          // Each partial sum of the gradients is a bf16 tensor in the graph.
           float g[8], g2[8];
           unpack8(gdy[k], g);
           unpack8(*reinterpret_cast<const uint4*>(st + 2 * row_bytes + c * 16), g2);
 #pragma unroll
           for (int e = 0; e < 8; ++e) g[e] += g2[e];
           gdy[k] = pack8(g);
+          if (has3) {
+            unpack8(gdy[k], g);
+            unpack8(*reinterpret_cast<const uint4*>(st + 3 * row_bytes + c * 16), g2);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) g[e] += g2[e];
+            gdy[k] = pack8(g);
+          }
         }
-        if (HAS_DRES)
-          gdr[k] = *reinterpret_cast<const uint4*>(st + (HAS_DY2 ? 3 : 2) * row_bytes + c * 16);
+        if (HAS_DRES)  // dres is the last row of the stage
+          gdr[k] = *reinterpret_cast<const uint4*>(st + (nin - 1) * row_bytes + c * 16);
       } else {
         gdy[k] = gx[k] = gdr[k] = make_uint4(0, 0, 0, 0);
       }
@@ -575,6 +596,7 @@ rmsnorm_bwd_generic_dx(BwdIn p, int64_t N, float eps) {
   for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
     float g = bf16_to_f(p.dy[base + n]);
     if (HAS_DY2) g = round_bf16(g + bf16_to_f(p.dy2[base + n]));
+    if (HAS_DY2 && p.dy3) g = round_bf16(g + bf16_to_f(p.dy3[base + n]));
     const float xf = bf16_to_f(p.x[base + n]);
     if (RECOMPUTE) s1 = fmaf(xf, xf, s1);
     s2 = fmaf(xf, g * bf16_to_f(p.w[n]), s2);
@@ -587,6 +609,7 @@ rmsnorm_bwd_generic_dx(BwdIn p, int64_t N, float eps) {
   for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
     float g = bf16_to_f(p.dy[base + n]);
     if (HAS_DY2) g = round_bf16(g + bf16_to_f(p.dy2[base + n]));
+    if (HAS_DY2 && p.dy3) g = round_bf16(g + bf16_to_f(p.dy3[base + n]));
     const float xhat = bf16_to_f(p.x[base + n]) * r;
     const float dx = (g * bf16_to_f(p.w[n]) - xhat * cmean) * r;
     const float o = HAS_DRES ? bf16_to_f(p.dres[base + n]) + round_bf16(dx) : dx;
@@ -607,6 +630,7 @@ rmsnorm_bwd_generic_dw(BwdIn p, int64_t M, int64_t N, int64_t rows_per_block) {
     const size_t i = static_cast<size_t>(row) * N + col;
     float g = bf16_to_f(p.dy[i]);
     if (HAS_DY2) g = round_bf16(g + bf16_to_f(p.dy2[i]));
+    if (HAS_DY2 && p.dy3) g = round_bf16(g + bf16_to_f(p.dy3[i]));
     acc = fmaf(g, bf16_to_f(p.x[i]) * p.rws[row], acc);
   }
   p.partials[static_cast<size_t>(blockIdx.y) * N + col] = acc;
@@ -740,8 +764,8 @@ int launch_bwd_t(const BwdPlan& pl, BwdIn p, int64_t M, int64_t N, float eps, cu
   const dim3 grid(static_cast<unsigned>(pl.G));
   const int T = pl.cfg.threads;
   if (pl.tma) {
-    constexpr int NIN = 2 + (HAS_DY2 ? 1 : 0) + (HAS_DRES ? 1 : 0);
-    const int stage_bytes = NIN * static_cast<int>(N) * 2;
+    const int nin = 2 + (HAS_DY2 ? 1 : 0) + (HAS_DY2 && p.dy3 ? 1 : 0) + (HAS_DRES ? 1 : 0);
+    const int stage_bytes = nin * static_cast<int>(N) * 2;
     const int S = std::min(8, (220 * 1024 / pl.cps - 1024) / stage_bytes);
     auto kern = pl.cfg.vpt == 1 ? rmsnorm_bwd_tma<1, HAS_DY2, HAS_DRES, RECOMPUTE>
                                 : rmsnorm_bwd_tma<2, HAS_DY2, HAS_DRES, RECOMPUTE>;
@@ -751,7 +775,7 @@ int launch_bwd_t(const BwdPlan& pl, BwdIn p, int64_t M, int64_t N, float eps, cu
                                  device_error_word());
       return check_launch();
     }
-    return FRAG_ERR_SHAPE;
+    // no room for the ring: the register-prefetch kernel on the same blocks
   }
   switch (pl.cfg.vpt) {
     case 2:
@@ -815,7 +839,16 @@ int frag_rmsnorm_bwd(const void* dy, const void* dy2, const void* x, const float
                      const void* w, const void* dres, void* dx_out, float* dw, void* dw_bf16,
                      int64_t M, int64_t N, float eps, void* workspace,
                      size_t workspace_bytes, frag_stream_t stream) {
+  return frag_rmsnorm_bwd3(dy, dy2, nullptr, x, rstd, w, dres, dx_out, dw, dw_bf16, M, N, eps,
+                           workspace, workspace_bytes, stream);
+}
+
+int frag_rmsnorm_bwd3(const void* dy, const void* dy2, const void* dy3, const void* x,
+                      const float* rstd, const void* w, const void* dres, void* dx_out, float* dw,
+                      void* dw_bf16, int64_t M, int64_t N, float eps, void* workspace,
+                      size_t workspace_bytes, frag_stream_t stream) {
   if (M < 0 || N < 0) return FRAG_ERR_INVALID_ARG;
+  if (dy3 && !dy2) return FRAG_ERR_INVALID_ARG;
   if (N == 0 && M > 0) return FRAG_ERR_SHAPE;
   if (M > 0 && (!dy || !x || !w || !dx_out)) return FRAG_ERR_INVALID_ARG;
   if (M > 0x7fffffffLL || N > 0x7fffffffLL) return FRAG_ERR_SHAPE;
@@ -830,6 +863,7 @@ int frag_rmsnorm_bwd(const void* dy, const void* dy2, const void* x, const float
   }
   bool aligned = aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx_out);
   if (dy2) aligned = aligned && aligned16(dy2);
+  if (dy3) aligned = aligned && aligned16(dy3);
   if (dres) aligned = aligned && aligned16(dres);
   const BwdPlan pl = make_bwd_plan(M, N, aligned);
   if (!workspace || workspace_bytes < bwd_workspace_bytes(pl, M, N)) return FRAG_ERR_WORKSPACE;
@@ -838,6 +872,7 @@ int frag_rmsnorm_bwd(const void* dy, const void* dy2, const void* x, const float
   BwdIn p;
   p.dy = static_cast<const uint16_t*>(dy);
   p.dy2 = static_cast<const uint16_t*>(dy2);
+  p.dy3 = static_cast<const uint16_t*>(dy3);
   p.x = static_cast<const uint16_t*>(x);
   p.rstd = rstd;
   p.w = static_cast<const uint16_t*>(w);

@@ -179,12 +179,14 @@ def rmsnorm_bwd_num_blocks(M: int, N: int, device=None) -> int:
 
 def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,
                 weight: torch.Tensor, *, dy2: torch.Tensor | None = None,
+                dy3: torch.Tensor | None = None,
                 dres: torch.Tensor | None = None, eps: float = 1e-6,
                 dw_dtype: torch.dtype | None = torch.float32,
                 workspace: torch.Tensor | None = None, return_partials: bool = False):
     """RMSNorm backward.  Returns (dx, dw[, partials]).
 
     dy2   optional second gradient summed (in bf16) into dy first
+    dy3   optional third gradient (needs dy2): dy = bf16(bf16(dy + dy2) + dy3)
     rstd  saved rstd (fp32, one per row) or None to recompute it with eps
     dres  optional residual gradient added (in bf16) to dx
     dw    fp32 (dw_dtype=torch.float32), bf16, or None (not reduced)
@@ -199,7 +201,9 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,
     if dy.shape != x.shape:
         raise ValueError(f"dy {tuple(dy.shape)} and x {tuple(x.shape)} differ")
     _rows(dy, N, "dy")
-    for name, t in (("dy2", dy2), ("dres", dres)):
+    if dy3 is not None and dy2 is None:
+        raise ValueError("dy3 needs dy2 (the gradients are summed in order)")
+    for name, t in (("dy2", dy2), ("dy3", dy3), ("dres", dres)):
         if t is not None:
             _need(t, name, torch.bfloat16, dev)
             if t.shape != x.shape:
@@ -221,11 +225,14 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,
         if workspace is None or workspace.numel() < need:
             workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
         wc = weight.contiguous()
-        _lib.call("frag_rmsnorm_bwd", _ptr(dy), _ptr(dy2), _ptr(x), _ptr(rstd), _ptr(wc),
-                  _ptr(dres), _ptr(dx),
-                  _ptr(dw) if dw_dtype == torch.float32 else None,
-                  _ptr(dw) if dw_dtype == torch.bfloat16 else None,
-                  M, N, float(eps), _ptr(workspace), workspace.numel(), _stream(dev))
+        tail = (_ptr(x), _ptr(rstd), _ptr(wc), _ptr(dres), _ptr(dx),
+                _ptr(dw) if dw_dtype == torch.float32 else None,
+                _ptr(dw) if dw_dtype == torch.bfloat16 else None,
+                M, N, float(eps), _ptr(workspace), workspace.numel(), _stream(dev))
+        if dy3 is None:
+            _lib.call("frag_rmsnorm_bwd", _ptr(dy), _ptr(dy2), *tail)
+        else:
+            _lib.call("frag_rmsnorm_bwd3", _ptr(dy), _ptr(dy2), _ptr(dy3), *tail)
         if return_partials:
             G = int(lib.frag_rmsnorm_bwd_num_blocks(M, N)) if M else 0
             parts = workspace[: G * N * 4].view(torch.float32).view(G, N)

@@ -16,9 +16,8 @@ for a failed launch), as the reference harness expects.  Inputs are never
 modified; outputs are new tensors on the inputs' device.
 
 Problems whose graphs are outside the library's ops are not registered:
-v7/0f38bc55457c returns q in fp32, v7/ed20955ec34b sums three gradients, and
-v8/43f0c930291e, v8/7e38211c7f1c are broken in the reference itself (their
-inputs do not match their graphs).  v8/f6251e84e3fa is broken the same way
+v7/0f38bc55457c returns q in fp32, and v8/43f0c930291e, v8/7e38211c7f1c are
+broken in the reference itself (their inputs do not match their graphs).  v8/f6251e84e3fa is broken the same way
 (its first input should be the (y, rstd) pair of a _fused_rms_norm); its
 drop-in is registered and works when given that pair.
 """
@@ -123,6 +122,20 @@ def add_rms_bwd_d8f596b3df34(mm_664, mm_666, add_recomputed, getitem_12_recomput
                                _unsafe_view_428, dy2=mm_666.contiguous().view(x.shape),
                                dres=add_218.contiguous(), dw_dtype=torch.float32)
     return dres.view(-1, N), dw
+
+
+def add3_rms_bwd_ed20955ec34b(mm_672, view_1794, mm_674, embedding, getitem_1_recomputed,
+                              _unsafe_view_432, add_220):
+    """v7/ed20955ec34b/optimized_kernel.py:118: dy = view_1794 + mm_672 + mm_674
+    (each partial sum bf16), backward against embedding with the saved rstd,
+    d_res = add_220 + dx (bf16), dweight fp32 -> (d_res like add_220, dweight fp32)."""
+    x = embedding.contiguous()
+    dres, dw = ops.rmsnorm_bwd(view_1794.contiguous(), x,
+                               getitem_1_recomputed.contiguous().view(x.shape[:-1]),
+                               _unsafe_view_432, dy2=mm_672.contiguous().view(x.shape),
+                               dy3=mm_674.contiguous().view(x.shape),
+                               dres=add_220.contiguous(), dw_dtype=torch.float32)
+    return dres, dw
 
 
 # ---------------------------------------------------------------- embedding
@@ -303,6 +316,7 @@ PROBLEMS: dict[str, Callable] = {
     "v7/45990c83cfd6": rms_bwd_45990c83cfd6,
     "v7/7f544ceb2120": add_rms_bwd_7f544ceb2120,
     "v8/d8f596b3df34": add_rms_bwd_d8f596b3df34,
+    "v7/ed20955ec34b": add3_rms_bwd_ed20955ec34b,
     "v7/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v6/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v5/1e49beb8a123": emb_fwd_1e49beb8a123,

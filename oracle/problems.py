@@ -83,6 +83,14 @@ def add_rms_bwd_d8f596b3df34(mm_664, mm_666, h, rstd, w, add_218):
     return (out.view(8192, 4096), aten._to_copy.default(dw, dtype=torch.float32))
 
 
+def add3_rms_bwd_ed20955ec34b(mm_672, view_1794, mm_674, embedding, rstd, w, add_220):
+    """v7/ed20955ec34b/problem.py:19-44: dy = add(add(view_1794, mm_672), mm_674)."""
+    dy = aten.add.Tensor(view_1794, aten.view.default(mm_672, [1, 8192, 4096]))
+    dy = aten.add.Tensor(dy, aten.view.default(mm_674, [1, 8192, 4096]))
+    dx, dw = F.rmsnorm_bwd(dy, embedding, rstd, w)
+    return (aten.add.Tensor(add_220, dx), aten._to_copy.default(dw, dtype=torch.float32))
+
+
 def emb_fwd_1e49beb8a123(flat, ids):
     """v7/1e49beb8a123/problem.py:16-23."""
     return F.embedding_fwd(flat.view(128256, 4096), ids)
@@ -220,6 +228,7 @@ ORACLES = {
     "v7/45990c83cfd6": rms_bwd_45990c83cfd6,
     "v7/7f544ceb2120": add_rms_bwd_7f544ceb2120,
     "v8/d8f596b3df34": add_rms_bwd_d8f596b3df34,
+    "v7/ed20955ec34b": add3_rms_bwd_ed20955ec34b,
     "v7/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v6/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v5/1e49beb8a123": emb_fwd_1e49beb8a123,

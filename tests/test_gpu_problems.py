@@ -29,7 +29,7 @@ pytestmark = pytest.mark.gpu
 FIXTURES = sorted(GOLDEN.glob("v*_*.pt"))
 
 EXACT = {"v7/1e49beb8a123", "v6/1e49beb8a123", "v5/1e49beb8a123", "v4/1e49beb8a123"}
-RMS_BWD = {"v7/45990c83cfd6", "v7/7f544ceb2120", "v8/d8f596b3df34"}
+RMS_BWD = {"v7/45990c83cfd6", "v7/7f544ceb2120", "v8/d8f596b3df34", "v7/ed20955ec34b"}
 EMB_BWD = {"v7/a12a160cb11b"}
 # norm -> embedding backward chain: output index of (dweight, table gradient)
 CHAIN = {"v6/0b493aad68f0": (3, 4), "v5/118d525f44e0": (3, 4), "v4/680e4c57cdc8": (3, 4),
@@ -67,6 +67,11 @@ def _dw_f64(key, cpu_in):
         x, w, dy = cpu_in
         _, rstd = F.rmsnorm_fwd(x, w, 1e-5)
         return F.rmsnorm_dw_f64(dy, x, rstd), (dy, x, rstd)
+    if key == "v7/ed20955ec34b":
+        mm_672, view_1794, mm_674, h, rstd, w, _ = cpu_in
+        dy = torch.ops.aten.add.Tensor(view_1794, mm_672.view(h.shape))
+        dy = torch.ops.aten.add.Tensor(dy, mm_674.view(h.shape))
+        return F.rmsnorm_dw_f64(dy, h, rstd), (dy, h, rstd)
     if key == "v7/7f544ceb2120":
         mm_666, view_1776, h, rstd, w, _ = cpu_in
         dy = torch.ops.aten.add.Tensor(view_1776, mm_666.view(h.shape))

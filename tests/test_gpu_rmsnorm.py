@@ -99,6 +99,26 @@ def test_rmsnorm_bwd(shape, variant):
     assert_f32_close(dw, ref, "dw", atol=_dw_atol(g, x, rstd))
 
 
+@pytest.mark.parametrize("shape", [(4, 2048, 4096), (33, 8192), (5, 1000)])
+@pytest.mark.parametrize("rstd_saved", [True, False])
+def test_rmsnorm_bwd_three_gradients(shape, rstd_saved):
+    """dy = bf16(bf16(dy + dy2) + dy3) (v7/ed20955ec34b), TMA ring and generic kernels."""
+    eps = 1e-5
+    x, w = _inputs(shape, seed=40)
+    dy, dy2, dy3, dres = (cf.randn(shape, seed=41 + j) for j in range(4))
+    _, rstd = ora.rmsnorm_fwd(x, w, eps)
+    r_arg = rstd.reshape(shape[:-1]).to(DEV) if rstd_saved else None
+    dx, dw = ops.rmsnorm_bwd(dy.to(DEV), x.to(DEV), r_arg, w.to(DEV), dy2=dy2.to(DEV),
+                             dy3=dy3.to(DEV), dres=dres.to(DEV), eps=eps)
+    g = torch.ops.aten.add.Tensor(torch.ops.aten.add.Tensor(dy, dy2), dy3)
+    edx, _ = ora.add_rmsnorm_bwd(g, None, x, rstd, w, dres)
+    # bf16(dres + bf16(dx)): a one-ulp difference in the rounded dx survives
+    # cancellation, so the bound scales with the summands
+    mag = (edx.float() - dres.float()).abs() + dres.float().abs()
+    assert_bf16_close(dx, edx, "d_res", atol=1e-2 + 1.6e-2 * mag)
+    assert_f32_close(dw, ora.rmsnorm_dw_f64(g, x, rstd), "dw", atol=_dw_atol(g, x, rstd))
+
+
 def test_rmsnorm_bwd_deterministic():
     shape = (4, 2048, 4096)
     x, w = _inputs(shape, seed=20)
