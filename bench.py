@@ -52,7 +52,7 @@ DOMINANT = "C4B"  # largest share of the step; its main kernel is the roofline k
 # Fusions beyond the five configurations (SURVEY "next" rows), measured on request:
 #   C2N  embedding gather + RMSNorm fused (C2 ids/table, eps 1e-5)
 #   C3S  RoPE fwd writing q/k in the [B, H, S, D] layout attention reads (C3 shapes)
-NEXT = ["C2N", "C3S", "C2C", "C2U"]
+NEXT = ["C2N", "C3S", "C2C", "C2U", "C2S"]
 
 
 # ------------------------------------------------------------------ helpers
@@ -486,7 +486,32 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
         f.e2e = lambda h: _e2e_call(lambda xs: unfused(**xs), h)
         return f
 
-    builders = {"C2N": mk_c2n, "C3S": mk_c3s, "C2C": lambda: mk_chain("C2C"),
+    def mk_c2s():
+        # FSDP unshard of the embedding table out of the all-gather buffer plus
+        # the final add + RMSNorm with the gathered weight, at the shapes of
+        # the reference problem (v8/8e33a91b7364: buffer [525340672] viewed
+        # [8, -1], splits [512, 65667072], rows [8192, 4096])
+        M, N, W = 8192, 4096, 8
+        shard = 65667072
+        res = cf.randn((1, M, N), device=dev, seed=seed0 + 40)
+        x = cf.randn((M, N), device=dev, seed=seed0 + 41)
+        flat = cf.randn((W * (512 + shard),), device=dev, seed=seed0 + 42).view(W, -1)
+        table = torch.empty(W, shard, dtype=torch.bfloat16, device=dev)
+        y = torch.empty_like(res)
+
+        def step(res, x, flat, out=None, y=None):
+            w = ops.copy_rows(flat[:, :512]).view(-1)
+            _, yy, _ = ops.add_rmsnorm_fwd(res, x.view(res.shape), w, 1e-5, write_h=False,
+                                           save_rstd=False, y_out=y)
+            return yy, ops.copy_rows(flat[:, 512:], out=out)
+        f = Frag("C2S", "FSDP table unshard + add/RMSNorm [8192,4096] (8 shards of 65667072)", M,
+                 cf.bytes_add_rmsnorm_unshard(M, N, W, shard),
+                 [("unshard_add_rmsnorm", lambda: step(res, x, flat, out=table, y=y))])
+        f.host = dict(res=res, x=x, flat=flat)
+        f.e2e = lambda h: _e2e_call(lambda xs: step(xs["res"], xs["x"], xs["flat"]), h)
+        return f
+
+    builders = {"C2N": mk_c2n, "C3S": mk_c3s, "C2S": mk_c2s, "C2C": lambda: mk_chain("C2C"),
                 "C2U": lambda: mk_chain("C2U"), "C0F": mk_c0f, "C1B": lambda: mk_rms_bwd("C1B", C1, False, 3, False),
                 "C2F": lambda: mk_c2("C2F"), "C2B": lambda: mk_c2("C2B"),
                 "C3F": lambda: mk_c3("C3F"), "C3B": lambda: mk_c3("C3B"),

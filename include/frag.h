@@ -262,6 +262,20 @@ FRAG_API int frag_rmsnorm_embedding_bwd(const void* x, const void* w, const floa
                                         int32_t* status, frag_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
+ * Row-strided copy: dst + r*dst_stride <- src + r*src_stride, row_bytes bytes
+ * per row, for r in [0, rows) (strides in bytes; rows must not overlap).
+ * The FSDP unshard of a parameter out of the flat all-gather buffer:
+ * replaces the clone of the [8, 65667072] split of wait_tensor_969 (row
+ * stride 65667584) into the contiguous [128256, 4096] table in
+ *   v8/8e33a91b7364/problem.py:44-51 (drop-in v8/8e33a91b7364/optimized_kernel.py:99),
+ * and the [8, 512] weight-shard gathers (clone -> _unsafe_view [4096]) of
+ *   v8/8e33a91b7364/problem.py:23-32 and v7/215dd2e6a519/problem.py:16-22.
+ * 16-byte aligned pointers, strides and row_bytes take the vector kernel.
+ * ------------------------------------------------------------------------- */
+FRAG_API int frag_copy_rows(const void* src, int64_t src_stride, void* dst, int64_t dst_stride,
+                            int64_t rows, int64_t row_bytes, frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
  * Rotary position embedding on up to two tensors (q and k) in one launch.
  * Tensor i (i = 0, 1) is bf16 [B, S, H_i, D] addressed by element strides
  * (stride_b, stride_s, stride_h; the last dimension is contiguous), and is

@@ -85,6 +85,7 @@ SIGNATURES: dict[str, tuple] = {
     "frag_embedding_rmsnorm_fwd": (
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
     "frag_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64]),
+    "frag_copy_rows": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp]),
     "frag_rmsnorm_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "frag_rmsnorm_embedding_bwd": (
         _int,

@@ -122,6 +122,13 @@ def bytes_rmsnorm_embedding_bwd(T: int, D: int, rows: int, n_dy: int = 3, dres: 
             + rows * D * F32 + D * F32)
 
 
+def bytes_add_rmsnorm_unshard(M: int, N: int, world: int, shard: int) -> int:
+    # res, x read; y written (h and rstd are not outputs); the weight gathered
+    # from `world` strided pieces (read + write); the table copied out of the
+    # all-gather buffer (read + write of world * shard elements)
+    return 3 * M * N * BF16 + 2 * N * BF16 + 2 * world * shard * BF16
+
+
 def bytes_rope(T: int, Hq: int, Hk: int, D: int) -> int:
     return 2 * T * (Hq + Hk) * D * BF16 + T * I64
 

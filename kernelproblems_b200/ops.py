@@ -33,6 +33,7 @@ __all__ = [
     "embedding_rmsnorm_fwd",
     "embedding_bwd",
     "rmsnorm_embedding_bwd",
+    "copy_rows",
     "rope",
     "check_status",
     "reset_status",
@@ -414,6 +415,28 @@ def rmsnorm_embedding_bwd(x: torch.Tensor, weight: torch.Tensor, ids: torch.Tens
     if _SYNC_CHECK:
         check_status(dev)
     return G, dw, y, d_emb
+
+
+def copy_rows(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Contiguous copy of a 2-D tensor whose rows are contiguous but may be
+    strided apart (a split of an FSDP all-gather buffer viewed [world, -1]).
+    Returns a new [rows, cols] tensor (or fills `out`)."""
+    if not isinstance(src, torch.Tensor):
+        raise TypeError("src must be a torch.Tensor")
+    if not src.is_cuda:
+        raise ValueError("src must be a CUDA tensor")
+    if src.dim() != 2 or (src.shape[1] > 1 and src.stride(1) != 1):
+        raise ValueError("src must be 2-D with contiguous rows")
+    rows, cols = src.shape
+    if out is None:
+        out = torch.empty(rows, cols, dtype=src.dtype, device=src.device)
+    elif out.shape != src.shape or out.dtype != src.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous tensor of src's shape and dtype")
+    es = src.element_size()
+    with _on_device(src.device):
+        _lib.call("frag_copy_rows", _ptr(src), src.stride(0) * es, _ptr(out), cols * es, rows,
+                  cols * es, _stream(src.device))
+    return out
 
 
 # ------------------------------------------------------------------- RoPE

@@ -60,6 +60,20 @@ def _fsdp_weight(shard_view: torch.Tensor) -> torch.Tensor:
     return shard_view.contiguous().view(-1)
 
 
+def add_rms_unshard_8e33a91b7364(mm_223, add_62, wait_tensor_969):
+    """v8/8e33a91b7364/optimized_kernel.py:99 (v6, v7 same id): h = add_62 +
+    mm_223 (bf16), y = _fused_rms_norm(h, weight, 1e-5) with the weight the
+    [8, 512] split 0 of the all-gather buffer viewed [8, -1], and the
+    [8, 65667072] split 1 unsharded into a contiguous [128256, 4096] table ->
+    (y [M, N], table)."""
+    flat = wait_tensor_969.view(8, -1)
+    w = ops.copy_rows(flat[:, :512]).view(-1)
+    _, y, _ = ops.add_rmsnorm_fwd(add_62.contiguous(), mm_223.contiguous().view(add_62.shape), w,
+                                  1e-5, write_h=False, save_rstd=False)
+    table = ops.copy_rows(flat[:, 512:]).view(VOCAB, DIM)
+    return (y.view(-1, w.numel()), table)
+
+
 def rms_fwd_215dd2e6a519(getitem_1614, add_61):
     """v7/215dd2e6a519/problem.py:10-24: weight gathered from the FSDP shard
     view, _fused_rms_norm -> three [M,N] views of y."""
@@ -313,6 +327,9 @@ PROBLEMS: dict[str, Callable] = {
     "v7/ac3fb0b7281f": rms_fwd_ac3fb0b7281f,
     "v6/ac3fb0b7281f": rms_fwd_ac3fb0b7281f,
     "v8/7884328a5557": add_rms_fwd_7884328a5557,
+    "v8/8e33a91b7364": add_rms_unshard_8e33a91b7364,
+    "v7/8e33a91b7364": add_rms_unshard_8e33a91b7364,
+    "v6/8e33a91b7364": add_rms_unshard_8e33a91b7364,
     "v7/45990c83cfd6": rms_bwd_45990c83cfd6,
     "v7/7f544ceb2120": add_rms_bwd_7f544ceb2120,
     "v8/d8f596b3df34": add_rms_bwd_d8f596b3df34,

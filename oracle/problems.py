@@ -61,6 +61,19 @@ def add_rms_fwd_7884328a5557(mm_220, add_61, w):
     return (y2, y2)
 
 
+def add_rms_unshard_8e33a91b7364(mm_223, add_62, wait_tensor_969):
+    """v8/8e33a91b7364/problem.py:16-52: add -> split_with_sizes([512, 65667072])
+    of the buffer viewed [8, -1] -> _fused_rms_norm with the split-0 weight,
+    and the split-1 clone viewed [128256, 4096]."""
+    h = aten.add.Tensor(add_62, aten._unsafe_view.default(mm_223, [1, 8192, 4096]))
+    parts = aten.split_with_sizes.default(aten.view.default(wait_tensor_969, [8, -1]), [512, 65667072], 1)
+    w = aten._unsafe_view.default(aten.clone.default(parts[0], memory_format=torch.contiguous_format), [4096])
+    y, _ = F.rmsnorm_fwd(h, w, 1e-5)
+    table = aten._unsafe_view.default(aten.clone.default(parts[1], memory_format=torch.contiguous_format),
+                                      [128256, 4096])
+    return (aten.view.default(y, [8192, 4096]), table)
+
+
 def rms_bwd_45990c83cfd6(x, w, dy):
     """v7/45990c83cfd6/problem.py:17-27."""
     dx, dw = F.rmsnorm_recompute_bwd(x, w, dy, 1e-5)
@@ -225,6 +238,9 @@ ORACLES = {
     "v7/ac3fb0b7281f": rms_fwd_ac3fb0b7281f,
     "v6/ac3fb0b7281f": rms_fwd_ac3fb0b7281f,
     "v8/7884328a5557": add_rms_fwd_7884328a5557,
+    "v8/8e33a91b7364": add_rms_unshard_8e33a91b7364,
+    "v7/8e33a91b7364": add_rms_unshard_8e33a91b7364,
+    "v6/8e33a91b7364": add_rms_unshard_8e33a91b7364,
     "v7/45990c83cfd6": rms_bwd_45990c83cfd6,
     "v7/7f544ceb2120": add_rms_bwd_7f544ceb2120,
     "v8/d8f596b3df34": add_rms_bwd_d8f596b3df34,

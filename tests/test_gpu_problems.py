@@ -31,6 +31,7 @@ FIXTURES = sorted(GOLDEN.glob("v*_*.pt"))
 EXACT = {"v7/1e49beb8a123", "v6/1e49beb8a123", "v5/1e49beb8a123", "v4/1e49beb8a123"}
 RMS_BWD = {"v7/45990c83cfd6", "v7/7f544ceb2120", "v8/d8f596b3df34", "v7/ed20955ec34b"}
 EMB_BWD = {"v7/a12a160cb11b"}
+UNSHARD = {"v8/8e33a91b7364", "v7/8e33a91b7364", "v6/8e33a91b7364"}  # output 1: a copy
 # norm -> embedding backward chain: output index of (dweight, table gradient)
 CHAIN = {"v6/0b493aad68f0": (3, 4), "v5/118d525f44e0": (3, 4), "v4/680e4c57cdc8": (3, 4),
          "v8/f6251e84e3fa": (0, 1)}
@@ -99,6 +100,9 @@ def test_problem_drop_in(fixture):
         o2 = oc.reshape(-1, oc.shape[-1]) if oc.dim() > 1 else oc.reshape(1, -1)
         if key in EXACT:
             assert torch.equal(oc, e), "embedding gather must be bit exact"
+            assert torch.equal(o2[rows], g["values"]), "golden rows"
+        elif key in UNSHARD and i == 1:
+            assert torch.equal(oc, e), "unsharded table must be bit exact"
             assert torch.equal(o2[rows], g["values"]), "golden rows"
         elif key in EMB_BWD:
             ids = cpu_in[1]
