@@ -66,7 +66,7 @@ def parse_args(argv=None):
     ap.add_argument("--workload", default="suite",
                     help="suite | next | emb_vp | one fragment of " + ",".join(SUITE + NEXT))
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0,
                     help="target CPU time of the cpu_baseline sample")
@@ -519,21 +519,49 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
     return [builders[n]() for n in SUITE + NEXT if n in names]
 
 
-def _e2e_call(fn, host):
+# (h2d stream, d2h stream) while e2e_measure runs, else None
+_E2E_PIPE = None
+
+
+def _e2e_call(fn, host, pipe=None):
     """Copy `host` (pinned) inputs to the device, run the public API call, copy
-    every output tensor back into pinned memory.  Returns (h2d, d2h) bytes."""
+    every output tensor back into pinned memory.  Returns (h2d, d2h) bytes.
+
+    With `pipe` = (h2d stream, d2h stream) the uploads and read-backs run on
+    their own streams, ordered by stream waits: the call waits for its own
+    uploads, the read-back waits for the call.  Consecutive calls then overlap
+    one call's read-back, the next call's kernels and the one after's upload
+    (the copy engines work in both directions at once)."""
     dev = torch.device("cuda", torch.cuda.current_device())
-    xs = {k: v.to(dev, non_blocking=True) for k, v in host["in"].items()}
+    cur = torch.cuda.current_stream(dev)
+    pipe = pipe if pipe is not None else _E2E_PIPE
+    if pipe is None:
+        xs = {k: v.to(dev, non_blocking=True) for k, v in host["in"].items()}
+    else:
+        h2d_s, d2h_s = pipe
+        with torch.cuda.stream(h2d_s):
+            xs = {k: v.to(dev, non_blocking=True) for k, v in host["in"].items()}
+        cur.wait_stream(h2d_s)
+        for t in xs.values():
+            t.record_stream(cur)
     outs = fn(xs)
     outs = outs if isinstance(outs, (tuple, list)) else (outs,)
     h2d = sum(v.numel() * v.element_size() for v in host["in"].values())
     d2h = 0
-    for i, o in enumerate(o for o in outs if isinstance(o, torch.Tensor)):
+    tensors = [o for o in outs if isinstance(o, torch.Tensor)]
+    if pipe is not None:
+        d2h_s.wait_stream(cur)
+    for i, o in enumerate(tensors):
         buf = host["out"].get(i)
         if buf is None or buf.shape != o.shape or buf.dtype != o.dtype:
             buf = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
             host["out"][i] = buf
-        buf.copy_(o, non_blocking=True)
+        if pipe is None:
+            buf.copy_(o, non_blocking=True)
+        else:
+            o.record_stream(d2h_s)
+            with torch.cuda.stream(d2h_s):
+                buf.copy_(o, non_blocking=True)
         d2h += o.numel() * o.element_size()
     return h2d, d2h
 
@@ -806,32 +834,47 @@ def ours_arm(args, rank, local_rank, world):
 
 
 def e2e_measure(frags, steps, world, dev, step_bytes):
+    """Every step: each fragment's inputs uploaded from pinned host memory, the
+    public API call, every output read back into pinned host memory.  Uploads
+    and read-backs run on their own streams (see _e2e_call), so one
+    fragment's read-back overlaps the next fragment's kernels and upload."""
+    global _E2E_PIPE
     hosts = {}
     for f in frags:
         hosts[f.name] = {"in": {k: v.detach().cpu().pin_memory() for k, v in f.host.items()}, "out": {}}
     stream = torch.cuda.current_stream(dev)
-    # warm-up (allocator, pinned output buffers)
-    for f in frags:
-        f.e2e(hosts[f.name])
-        if f.exchange is not None:
-            f.exchange()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    h2d = d2h = 0
-    a.record(stream)
-    for _ in range(steps):
-        h2d = d2h = 0
+    h2d_s = torch.cuda.Stream(dev)
+    d2h_s = torch.cuda.Stream(dev)
+    _E2E_PIPE = (h2d_s, d2h_s)
+    try:
+        # warm-up (allocator, pinned output buffers)
         for f in frags:
-            i, o = f.e2e(hosts[f.name])
+            f.e2e(hosts[f.name])
             if f.exchange is not None:
                 f.exchange()
-            h2d += i
-            d2h += o
-    b.record(stream)
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        h2d = d2h = 0
+        a.record(stream)
+        h2d_s.wait_stream(stream)  # no copy starts before the start event
+        d2h_s.wait_stream(stream)
+        for _ in range(steps):
+            h2d = d2h = 0
+            for f in frags:
+                i, o = f.e2e(hosts[f.name])
+                if f.exchange is not None:
+                    f.exchange()
+                h2d += i
+                d2h += o
+        stream.wait_stream(h2d_s)  # the end event follows every copy
+        stream.wait_stream(d2h_s)
+        b.record(stream)
+        torch.cuda.synchronize()
+    finally:
+        _E2E_PIPE = None
     ms = a.elapsed_time(b) / steps
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -841,7 +884,8 @@ def e2e_measure(frags, steps, world, dev, step_bytes):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
             "steps": steps,
             "path": "kernelproblems_b200.ops public API, inputs from pinned host memory, "
-                    "every output copied back to pinned host memory"}
+                    "every output copied back to pinned host memory; uploads and read-backs on "
+                    "their own streams, overlapping neighbouring fragments' kernels"}
 
 
 def emb_vp_arm(args, rank, world, dev, pg):
