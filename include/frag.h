@@ -285,8 +285,12 @@ FRAG_API int frag_copy_rows(const void* src, int64_t src_stride, void* dst, int6
  *                   (fp32, cos/sin evaluated in registers; nothing is read
  *                   from HBM besides x and the positions)
  *   freqs != NULL : (cos, sin) := (re, im) of freqs[p, j], a complex64 table
- *                   of row stride freqs_stride (in complex elements) — the
- *                   reference's freqs_cis input (not necessarily unit modulus).
+ *                   of freqs_rows rows of stride freqs_stride (in complex
+ *                   elements) — the reference's freqs_cis input (not
+ *                   necessarily unit modulus).  A position outside
+ *                   [0, freqs_rows) is not read: it sets
+ *                   FRAG_DEVFLAG_INDEX_OOB in the library's error word
+ *                   (frag_device_errors) and its token is copied unrotated.
  * layout NEOX rotates (x_j, x_{j+D/2}); INTERLEAVED rotates (x_2j, x_2j+1).
  * inverse != 0 rotates by the conjugate (the backward of RoPE).
  * Positions p = pos[b*pos_stride_b + s*pos_stride_s] (int32 or int64), or s.
@@ -306,8 +310,16 @@ typedef struct frag_rope_tensor {
 FRAG_API int frag_rope(const frag_rope_tensor* tensors, int num_tensors, int64_t B,
               int64_t S, int64_t D, const void* pos, int pos_dtype,
               int64_t pos_stride_b, int64_t pos_stride_s, const float* freqs,
-              int64_t freqs_stride, float theta, int layout, int inverse,
-              frag_stream_t stream);
+              int64_t freqs_stride, int64_t freqs_rows, float theta, int layout,
+              int inverse, frag_stream_t stream);
+
+/* Self-test of the bounded waits: one thread waits limit_cycles
+ * (0 < limit_cycles <= 4e9) on an mbarrier that nothing arrives on, with the
+ * same wait every TMA kernel here uses.  The wait gives up and sets
+ * FRAG_DEVFLAG_WAIT_TIMEOUT in the error word (frag_device_errors); the
+ * context stays usable.  No counterpart in the reference, which has no
+ * device-side waits. */
+FRAG_API int frag_selftest_bounded_wait(int64_t limit_cycles, frag_stream_t stream);
 
 /* Device properties the host layer uses to size launches and workspaces. */
 FRAG_API int frag_device_sm_count(void);

@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple] = {
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
     "frag_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64]),
     "frag_copy_rows": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp]),
+    "frag_selftest_bounded_wait": (_int, [_i64, _vp]),
     "frag_rmsnorm_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "frag_rmsnorm_embedding_bwd": (
         _int,
@@ -98,8 +99,8 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "frag_rope": (
         _int,
-        [C.POINTER(RopeTensor), _int, _i64, _i64, _i64, _vp, _int, _i64, _i64, _vp, _i64, _f32,
-         _int, _int, _vp],
+        [C.POINTER(RopeTensor), _int, _i64, _i64, _i64, _vp, _int, _i64, _i64, _vp, _i64, _i64,
+         _f32, _int, _int, _vp],
     ),
 }
 

@@ -211,17 +211,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for phase `parity` of `bar` to complete; false (and the error bit set)
-// if it has not after kWaitCycles.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// if it has not after `limit` clock cycles.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err,
+                                              long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       if (err) atomicOr(err, FRAG_DEVFLAG_WAIT_TIMEOUT);
       return false;
     }
   }
   return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  return mbar_wait_for(bar, parity, err, kWaitCycles);
 }
 // Global -> shared bulk copy of `bytes` (multiple of 16, both addresses
 // 16-byte aligned), completing on `bar`.

@@ -46,6 +46,8 @@ struct RopeP {
   int64_t psb, pss;
   const float* freqs;  // complex64 as (re, im) float pairs
   int64_t fstride;     // complex elements per table row
+  int64_t frows;       // table rows: positions outside [0, frows) are flagged
+  int* err;            // library error word (FRAG_DEVFLAG_INDEX_OOB)
   float sign;          // +1 forward, -1 inverse
   float inv_freq[kMaxHalf];
 };
@@ -102,11 +104,22 @@ __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
   const int64_t b = tok / p.S, s = tok - b * p.S;
   const int64_t pos = load_pos(p, b, s);
   const int j = lane % LPH, hs = lane / LPH;
+  // A position outside the table is an input error (the reference's
+  // freqs_cis[pos] raises): flag it and rotate by nothing instead of
+  // reading outside the table.
+  const bool bad = TABLE && (pos < 0 || pos >= p.frows);
+  if (bad && lane == 0 && p.err) atomicOr(p.err, FRAG_DEVFLAG_INDEX_OOB);
 
   // Frequency index of pair i (0..7) of this lane.
   auto fidx = [&](int i) { return NEOX ? 8 * j + i : (i < 4 ? 4 * j + i : (half >> 1) + 4 * j + i - 4); };
   float cs[8], sn[8];
-  if (TABLE) {
+  if (bad) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      cs[i] = 1.f;
+      sn[i] = 0.f;
+    }
+  } else if (TABLE) {
     // pairs i = 0..3 and 4..7 are 4 consecutive complex values each
     const float* row = p.freqs + 2 * pos * p.fstride;
 #pragma unroll
@@ -173,6 +186,8 @@ __global__ void __launch_bounds__(256) rope_generic(const RopeP p) {
   const int64_t tok = blockIdx.x;
   const int64_t b = tok / p.S, s = tok - b * p.S;
   const int64_t pos = load_pos(p, b, s);
+  const bool bad = TABLE && (pos < 0 || pos >= p.frows);  // flagged, no table read
+  if (bad && threadIdx.x == 0 && p.err) atomicOr(p.err, FRAG_DEVFLAG_INDEX_OOB);
 #pragma unroll
   for (int ti = 0; ti < 2; ++ti) {
     if (ti >= p.nt) break;
@@ -182,7 +197,10 @@ __global__ void __launch_bounds__(256) rope_generic(const RopeP p) {
     for (int64_t q = threadIdx.x; q < static_cast<int64_t>(T.H) * half; q += blockDim.x) {
       const int h = static_cast<int>(q / half), jj = static_cast<int>(q - static_cast<int64_t>(h) * half);
       float cv, sv;
-      if (TABLE) {
+      if (bad) {
+        cv = 1.f;
+        sv = 0.f;
+      } else if (TABLE) {
         cv = p.freqs[2 * (pos * p.fstride + jj)];
         sv = p.freqs[2 * (pos * p.fstride + jj) + 1];
       } else {
@@ -229,7 +247,8 @@ using namespace frag;
 extern "C" int frag_rope(const frag_rope_tensor* tensors, int num_tensors, int64_t B, int64_t S,
                          int64_t D, const void* pos, int pos_dtype, int64_t pos_stride_b,
                          int64_t pos_stride_s, const float* freqs, int64_t freqs_stride,
-                         float theta, int layout, int inverse, frag_stream_t stream) {
+                         int64_t freqs_rows, float theta, int layout, int inverse,
+                         frag_stream_t stream) {
   if (!tensors || num_tensors < 1 || num_tensors > 2) return FRAG_ERR_INVALID_ARG;
   if (B < 0 || S < 0 || D < 0) return FRAG_ERR_INVALID_ARG;
   if (layout != FRAG_ROPE_NEOX && layout != FRAG_ROPE_INTERLEAVED) return FRAG_ERR_INVALID_ARG;
@@ -249,8 +268,11 @@ extern "C" int frag_rope(const frag_rope_tensor* tensors, int num_tensors, int64
   p.pos_dtype = pos_dtype;
   p.psb = pos_stride_b;
   p.pss = pos_stride_s;
+  if (freqs && freqs_rows < 0) return FRAG_ERR_INVALID_ARG;
   p.freqs = freqs;
   p.fstride = freqs_stride;
+  p.frows = freqs_rows;
+  p.err = freqs ? device_error_word() : nullptr;
   p.sign = inverse ? -1.0f : 1.0f;
   const int half = static_cast<int>(D / 2);
   for (int i = 0; i < kMaxHalf; ++i) p.inv_freq[i] = 0.f;

@@ -84,9 +84,32 @@ bool allow_dynamic_smem(const void* kernel, int bytes) {
   return true;
 }
 
+namespace {
+
+// One thread waits, with the library's bounded wait, on an mbarrier that
+// nothing arrives on: the wait must give up after `limit` cycles and set
+// FRAG_DEVFLAG_WAIT_TIMEOUT in the error word, as every kernel's waits do.
+__global__ void bounded_wait_probe(int* err, long long limit) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  mbar_init_fence();
+  mbar_wait_for(&bar, 0, err, limit);
+}
+
+}  // namespace
 }  // namespace frag
 
 extern "C" {
+
+int frag_selftest_bounded_wait(int64_t limit_cycles, frag_stream_t stream) {
+  if (limit_cycles <= 0 || limit_cycles > frag::kWaitCycles) return FRAG_ERR_INVALID_ARG;
+  int* err = frag::device_error_word();
+  if (!err) return FRAG_ERR_CUDA;
+  frag::bounded_wait_probe<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      err, static_cast<long long>(limit_cycles));
+  return frag::check_launch();
+}
 
 const char* frag_version(void) { return "libfrag 0.1.0 (sm_100a)"; }
 

@@ -84,7 +84,8 @@ def _status_word(dev: torch.device) -> torch.Tensor:
 
 
 def check_status(device: torch.device | int | None = None) -> None:
-    """Synchronise and raise IndexError if a kernel flagged an out-of-range id,
+    """Synchronise and raise IndexError if a kernel flagged an out-of-range id
+    (embedding ids, RoPE table positions),
     RuntimeError if a kernel gave up waiting for its own copies (a bounded
     wait expired: its outputs are not valid)."""
     lib = _lib.load()
@@ -96,6 +97,8 @@ def check_status(device: torch.device | int | None = None) -> None:
         raise FragError("frag_device_errors", -flags)
     if flags & _lib.FRAG_DEVFLAG_WAIT_TIMEOUT:
         raise RuntimeError("a libfrag kernel's bounded wait expired; its outputs are invalid")
+    if flags & _lib.FRAG_DEVFLAG_INDEX_OOB:
+        raise IndexError("rope: a position was outside the freqs table")
     devs = list(_status_words) if device is None else [torch.device("cuda", device).index
                                                         if isinstance(device, int) else device.index]
     for idx in devs:
@@ -515,14 +518,14 @@ def rope(q: torch.Tensor, k: torch.Tensor | None = None, positions: torch.Tensor
         else:
             raise ValueError(f"positions must be [B, S] or [S], got {tuple(positions.shape)}")
         pos_ptr = C.c_void_p(positions.data_ptr())
-    fptr, fstride = None, 0
+    fptr, fstride, frows = None, 0, 0
     if freqs is not None:
         if freqs.dtype != torch.complex64 or freqs.device != dev:
             raise TypeError("freqs must be a complex64 tensor on q's device")
         f2 = freqs.reshape(-1, freqs.shape[-1])
         if f2.shape[-1] != D // 2 or f2.stride(-1) != 1:
             raise ValueError(f"freqs rows must hold D/2={D // 2} contiguous complex values")
-        fptr, fstride = C.c_void_p(f2.data_ptr()), f2.stride(0)
+        fptr, fstride, frows = C.c_void_p(f2.data_ptr()), f2.stride(0), f2.shape[0]
         theta_v = 0.0
     else:
         if theta is None:
@@ -530,5 +533,5 @@ def rope(q: torch.Tensor, k: torch.Tensor | None = None, positions: torch.Tensor
         theta_v = float(theta)
     with _on_device(dev):
         _lib.call("frag_rope", arr, len(descs), B, S, D, pos_ptr, pos_dtype, psb, pss, fptr,
-                  fstride, theta_v, _LAYOUTS[layout], int(bool(inverse)), _stream(dev))
+                  fstride, frows, theta_v, _LAYOUTS[layout], int(bool(inverse)), _stream(dev))
     return oq, ok

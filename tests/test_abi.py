@@ -57,11 +57,11 @@ def test_invalid_arguments_rejected_on_host():
     assert lib.frag_embedding_fwd(null, null, null, 0, 4, 4, 0, 4, null, null) == 0
     assert lib.frag_embedding_bwd(null, null, null, -1, 4, 4, 0, 4, -1, null, 0, null, null) == 1
     assert lib.frag_dw_reduce(null, 1, 4, null, null, null) == 1
-    assert lib.frag_rope(None, 1, 1, 1, 128, null, 0, 0, 0, null, 0, 1e4, 0, 0, null) == 1
+    assert lib.frag_rope(None, 1, 1, 1, 128, null, 0, 0, 0, null, 0, 0, 1e4, 0, 0, null) == 1
     t = (_lib.RopeTensor * 1)(_lib.RopeTensor(0, 0, 1, 0, 0, 0, 0, 0, 0))
-    assert lib.frag_rope(t, 1, 1, 1, 128, null, 0, 0, 0, null, 0, 1e4, 7, 0, null) == 1  # bad layout
-    assert lib.frag_rope(t, 3, 1, 1, 128, null, 0, 0, 0, null, 0, 1e4, 0, 0, null) == 1  # > 2 tensors
-    assert lib.frag_rope(t, 1, 1, 1, 127, null, 0, 0, 0, null, 0, 1e4, 0, 0, null) == 2  # odd D
+    assert lib.frag_rope(t, 1, 1, 1, 128, null, 0, 0, 0, null, 0, 0, 1e4, 7, 0, null) == 1  # bad layout
+    assert lib.frag_rope(t, 3, 1, 1, 128, null, 0, 0, 0, null, 0, 0, 1e4, 0, 0, null) == 1  # > 2 tensors
+    assert lib.frag_rope(t, 1, 1, 1, 127, null, 0, 0, 0, null, 0, 0, 1e4, 0, 0, null) == 2  # odd D
 
 
 def test_fraggerror_message():

@@ -3,7 +3,8 @@ world size 2), with the CUDA kernels replaced by oracle functions: row
 sharding, the dweight exchange (all-gather + fixed-order sum, and plain
 all-reduce), the vocab-parallel embedding forward (masked gather +
 all-reduce) and backward (per-rank table-gradient shard), and host-side
-failure detection (a rank that raises before a collective)."""
+failure detection (a rank that raises before a collective, and a rank that
+stalls until the process group's timeout ends the other rank's collective)."""
 import datetime
 import os
 import socket
@@ -128,6 +129,24 @@ def _body_rank1_raises(rank):
     return t
 
 
+_STALL_S = 8.0
+
+
+def _body_rank1_stalls(rank):
+    """Rank 1 stays alive but never joins the collective: rank 0's collective
+    must end with an error once the process group's timeout expires."""
+    import time
+    if rank == 1:
+        time.sleep(_STALL_S)
+        return None
+    t0 = time.monotonic()
+    try:
+        dist.all_reduce(torch.ones(4))
+    except Exception as e:  # the expected outcome
+        return ("error", time.monotonic() - t0, f"{type(e).__name__}: {e}"[:200])
+    return ("completed", time.monotonic() - t0, "")
+
+
 # ---- tests ------------------------------------------------------------------
 
 @pytest.mark.parametrize("body", [_body_rms, _body_rms_allreduce])
@@ -171,3 +190,11 @@ def test_rank_failure_is_reported_not_hung():
     out = run_ranks(_body_rank1_raises, timeout_s=5)
     assert out[1][0] == "error" and "fails before" in out[1][1]
     assert out[0][0] == "error", "the surviving rank's collective must end with an error"
+
+
+def test_stalled_rank_ends_collective_by_timeout():
+    out = run_ranks(_body_rank1_stalls, timeout_s=3)
+    assert out[0][0] == "ok", out[0]
+    outcome, elapsed, msg = out[0][1]
+    assert outcome == "error", "the waiting rank's collective must fail, not complete"
+    assert elapsed < _STALL_S - 1.0, f"error came after {elapsed:.1f}s: the timeout did not end the wait"
