@@ -170,6 +170,20 @@ __device__ __forceinline__ float block_sum(float v, float (*slots)[32], int pari
   return t;
 }
 
+// Elementwise sum of two bf16x2 words rounded to bf16 (ties to even).  The
+// fp32 sum of two bf16 values rounded to bf16 (what an aten bf16 add
+// computes) is the correctly rounded bf16 sum, which is what the packed bf16
+// add gives: the two agree for every input.
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                             *reinterpret_cast<const __nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint4 add_bf16x8(const uint4& a, const uint4& b) {
+  return make_uint4(add_bf16x2(a.x, b.x), add_bf16x2(a.y, b.y), add_bf16x2(a.z, b.z),
+                    add_bf16x2(a.w, b.w));
+}
+
 // Round two fp32 values to the nearest bf16 (ties to even) with one packed
 // conversion and widen them back.
 __device__ __forceinline__ void round_bf16x2(float& a, float& b) {

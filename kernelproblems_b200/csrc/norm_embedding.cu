@@ -188,26 +188,16 @@ norm_emb_bwd_tma(ChainIn p, int S, int* err) {
       const bool in = c < chunks;
       const uint4 z = make_uint4(0, 0, 0, 0);
       R.x[k] = in ? *reinterpret_cast<const uint4*>(st + c * 16) : z;
-      float g[8];
-      unpack8(in ? *reinterpret_cast<const uint4*>(st + row_bytes + c * 16) : z, g);
+      // each partial sum of the gradients is a bf16 tensor in the graph:
+      // packed bf16 adds give exactly those sums
+      uint4 gp = in ? *reinterpret_cast<const uint4*>(st + row_bytes + c * 16) : z;
       int slot = 2;
-      if (p.dy1) {
-        // each partial sum of the gradients is a bf16 tensor in the graph
-        float g2[8];
-        unpack8(in ? *reinterpret_cast<const uint4*>(st + (slot++) * row_bytes + c * 16) : z, g2);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) g[e] += g2[e];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) round_bf16x2(g[e], g[e + 1]);
-      }
-      if (p.dy2) {
-        float g3[8];
-        unpack8(in ? *reinterpret_cast<const uint4*>(st + (slot++) * row_bytes + c * 16) : z, g3);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) g[e] += g3[e];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) round_bf16x2(g[e], g[e + 1]);
-      }
+      if (p.dy1)
+        gp = add_bf16x8(gp, in ? *reinterpret_cast<const uint4*>(st + (slot++) * row_bytes + c * 16) : z);
+      if (p.dy2)
+        gp = add_bf16x8(gp, in ? *reinterpret_cast<const uint4*>(st + (slot++) * row_bytes + c * 16) : z);
+      float g[8];
+      unpack8(gp, g);
       R.set_g(k, g);
       R.r[k] = (p.dres && in) ? *reinterpret_cast<const uint4*>(st + slot * row_bytes + c * 16) : z;
       float xf[8], wv[8];
@@ -265,7 +255,6 @@ norm_emb_bwd_tma(ChainIn p, int S, int* err) {
       unpack8(A.x[k], xf);
       A.get_g(k, g);
       weight(k, wv);
-      if (p.dres) unpack8(A.r[k], d);
       float dx[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -274,24 +263,17 @@ norm_emb_bwd_tma(ChainIn p, int S, int* err) {
         dx[e] = (g[e] * wv[e] - xhat * cmean) * r;
         dwacc[k][e] = fmaf(g[e], xhat, dwacc[k][e]);
       }
-#pragma unroll
-      for (int e = 0; e < 8; e += 2) round_bf16x2(dx[e], dx[e + 1]);
-      if (p.dres) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) d[e] += dx[e];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) round_bf16x2(d[e], d[e + 1]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) d[e] = dx[e];
-      }
+      // d_emb = bf16(dres + bf16(dx)): round dx, then one packed bf16 add
+      uint4 dp = pack8(dx);
+      if (p.dres) dp = add_bf16x8(A.r[k], dp);
+      unpack8(dp, d);
       if (in_shard) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) gacc[k][e] += d[e];
       }
       if (c < chunks) {
         if (p.y) st_global(p.y + base + c * 8, pack8(yv));
-        if (p.demb) st_global(p.demb + base + c * 8, pack8(d));
+        if (p.demb) st_global(p.demb + base + c * 8, dp);
       }
     }
     // end of a run: its table row (or a boundary slot) is written once
