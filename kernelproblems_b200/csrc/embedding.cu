@@ -534,8 +534,10 @@ int frag_embedding_bwd(const int64_t* ids, const void* grad, float* G, int64_t T
   if (D % 8 == 0 && units <= 4 * 128 && (reinterpret_cast<uintptr_t>(G) & 31) == 0 &&
       (Ti == 0 || aligned16(grad))) {
     EmbBwdFront f;
+    // one persistent wave of the sweep (8 x 256 threads per SM; measured
+    // faster than several waves of a larger grid, or fewer CTAs per SM)
     int st = emb_bwd_front(ids, Ti, shard_rows, D, vocab_lo, vocab_total, padding_idx, G,
-                           /*zero_sweep=*/true, /*zero_ctas_per_sm=*/32, /*sort_first=*/false, ws,
+                           /*zero_sweep=*/true, /*zero_ctas_per_sm=*/8, /*sort_first=*/false, ws,
                            L, status, s, &f);
     if (st == FRAG_OK && Ti > 0) {
       const int Di = static_cast<int>(D);
