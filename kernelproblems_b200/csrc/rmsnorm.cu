@@ -80,7 +80,7 @@ rmsnorm_fwd_vec(const uint16_t* __restrict__ x, const uint16_t* __restrict__ res
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[k][i] = round_bf16(r8[i] + v[k][i]);
       const int c = threadIdx.x + k * blockDim.x;
-      if (WRITE_H && c < chunks) st_global(h + base + c * 8, pack8(v[k]));
+      if (WRITE_H && c < chunks) st_stream(h + base + c * 8, pack8(v[k]));
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) ss = fmaf(v[k][i], v[k][i], ss);
@@ -97,7 +97,7 @@ rmsnorm_fwd_vec(const uint16_t* __restrict__ x, const uint16_t* __restrict__ res
       unpack8(wv[k], wf);
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = (v[k][i] * r) * wf[i];
-      st_global(y + base + c * 8, pack8(o));
+      st_stream(y + base + c * 8, pack8(o));  // evict-first: 0.6-1.5% faster (C4F, C0F)
     }
   }
 }
