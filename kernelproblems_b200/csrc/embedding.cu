@@ -2,8 +2,7 @@
 //
 // Forward (aten.embedding, v7/1e49beb8a123/problem.py:20-23): one warp per
 // token copies table[ids[t]] to out[t] with 128-bit loads/stores, all of a
-// row's loads issued before its stores (evict-first: measured 2% faster at
-// 32768 tokens than default-policy stores).  A vocab shard [vocab_lo,
+// row's loads issued before its stores.  A vocab shard [vocab_lo,
 // vocab_lo + shard_rows) writes zero rows for ids outside the shard, which is
 // the masked half of a vocab-parallel embedding (the other half is the
 // all-reduce done by the caller).  The copy is bit exact.
@@ -59,7 +58,7 @@ emb_fwd_vec(const int64_t* __restrict__ ids, const uint16_t* __restrict__ table,
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const int c = c0 + u * 32 + lane;
-      if (c < chunks) st_stream(dst + c * 8, buf[u]);  // output rows are not re-read here
+      if (c < chunks) st_global(dst + c * 8, buf[u]);
     }
   }
 }

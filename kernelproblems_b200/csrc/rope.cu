@@ -167,10 +167,8 @@ __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
         if (h < T.H) {
           uint4 ra, rc;
           rotate<NEOX>(va[u], vc[u], cs, sn, ra, rc);
-          // evict-first: the rotated heads are not re-read here (measured 2%
-          // faster than default-policy stores at the C3 shapes)
-          st_stream(ob + h * T.osh + oa, ra);
-          st_stream(ob + h * T.osh + oc, rc);
+          st_global(ob + h * T.osh + oa, ra);
+          st_global(ob + h * T.osh + oc, rc);
         }
       }
     }
