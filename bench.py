@@ -18,7 +18,9 @@ the 126 MB L2 without an explicit flush):
 `value` = algorithmic bytes of the step on all ranks / max-over-ranks device
 time per step (CUDA events on the launching stream, per-fragment CUDA graphs).
 At N>1 every rank runs its own batch (weak scaling); the only collective in
-the step is the dweight exchange of C1B and C4B.  The vocab-parallel embedding
+the step is the dweight exchange of C1B and C4B, which runs on its own
+stream beside the fragments that follow it (the per-fragment breakdown times
+it inline instead).  The vocab-parallel embedding
 (masked gather + NCCL all-reduce of the output) is `--workload emb_vp`.
 
 `--impl reference` times the reference's torch-eager CPU graph (restated in
@@ -206,6 +208,7 @@ class Step:
 
     def __init__(self, frags, use_graphs: bool):
         self.frags = frags
+        self.comm = None  # stream of the overlapped exchanges (N > 1)
         for f in frags:  # warm: load kernels, size workspaces, first launches
             for _, fn in f.stages:
                 fn()
@@ -252,6 +255,10 @@ class Step:
                     f.ev[si + 1].record()
 
     def _run(self, graphs, events):
+        main = torch.cuda.current_stream()
+        overlap = not events and any(seg[-1].exchange is not None for _, seg in graphs)
+        if overlap and self.comm is None:
+            self.comm = torch.cuda.Stream()
         for g, seg in graphs:
             if g is not None:
                 g.replay()
@@ -259,12 +266,26 @@ class Step:
                 self._launch(seg, events)
             last = seg[-1]
             if last.exchange is not None:
-                last.exchange()
+                if overlap:
+                    # The exchange (dweight all-gather + fixed-order sum) runs
+                    # on its own stream after this segment's kernels, beside
+                    # the following fragments, none of which reads its result;
+                    # the step waits for it at the end.
+                    done = torch.cuda.Event()
+                    done.record(main)
+                    self.comm.wait_event(done)
+                    with torch.cuda.stream(self.comm):
+                        last.exchange()
+                else:
+                    last.exchange()
                 if events:
                     last.ev_end.record()
+        if overlap:
+            main.wait_stream(self.comm)
 
     def run(self):
-        """One step as timed: no timing events inside."""
+        """One step as timed: no timing events inside; NCCL exchanges overlap
+        the fragments that follow them."""
         self._run(self.plain, events=False)
 
     def run_instrumented(self):
