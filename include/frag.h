@@ -65,6 +65,9 @@ enum frag_devflag {
  * INTERLEAVED pairs 2i with 2i+1 (complex view, the reference's layout). */
 enum frag_rope_layout { FRAG_ROPE_NEOX = 0, FRAG_ROPE_INTERLEAVED = 1 };
 
+/* RoPE output element types (frag_rope_tensor.out_dtype). */
+enum frag_rope_out { FRAG_ROPE_OUT_BF16 = 0, FRAG_ROPE_OUT_F32 = 1 };
+
 /* Position tensor dtypes for RoPE. NONE means position = token index s. */
 enum frag_pos_dtype { FRAG_POS_NONE = 0, FRAG_POS_I32 = 1, FRAG_POS_I64 = 2 };
 
@@ -279,7 +282,8 @@ FRAG_API int frag_copy_rows(const void* src, int64_t src_stride, void* dst, int6
  * Rotary position embedding on up to two tensors (q and k) in one launch.
  * Tensor i (i = 0, 1) is bf16 [B, S, H_i, D] addressed by element strides
  * (stride_b, stride_s, stride_h; the last dimension is contiguous), and is
- * written to out_i with its own strides.  in and out may alias exactly.
+ * written to out_i with its own strides (bf16, or fp32 when out_dtype says
+ * so).  A bf16 in and out may alias exactly.
  * Angle for pair j (0 <= j < D/2) at position p:
  *   freqs == NULL : theta_j = p * inv_freq[j], inv_freq[j] = theta^(-2j/D)
  *                   (fp32, cos/sin evaluated in registers; nothing is read
@@ -296,7 +300,8 @@ FRAG_API int frag_copy_rows(const void* src, int64_t src_stride, void* dst, int6
  * Positions p = pos[b*pos_stride_b + s*pos_stride_s] (int32 or int64), or s.
  * Replaces the complex-mul RoPE of v8/c8c60d8f7015/problem.py:18-70 (drop-in
  * v8/c8c60d8f7015/optimized_kernel.py:48), v8/97032595d968 (:44),
- * v8/e29b92927600 (:54), v8/493cad38cac9 (:48), and the backward fragments
+ * v8/e29b92927600 (:54), v8/493cad38cac9 (:48), v7/0f38bc55457c (fp32 q,
+ * drop-in v7/0f38bc55457c/optimized_kernel.py:84), and the backward fragments
  * v7/bfe872e373e4 (:54), v7/5c65f62b0422 (:45), v6/03d64c25b654 (:51).
  * ------------------------------------------------------------------------- */
 typedef struct frag_rope_tensor {
@@ -305,6 +310,10 @@ typedef struct frag_rope_tensor {
   int64_t H;
   int64_t x_stride_b, x_stride_s, x_stride_h;
   int64_t out_stride_b, out_stride_s, out_stride_h;
+  /* FRAG_ROPE_OUT_BF16 (0): out is bf16 (rounded once); FRAG_ROPE_OUT_F32
+   * (1): out is fp32, not rounded (v7/0f38bc55457c/problem.py:10-40 returns
+   * q that way); out strides are in elements of out's type. */
+  int32_t out_dtype;
 } frag_rope_tensor;
 
 FRAG_API int frag_rope(const frag_rope_tensor* tensors, int num_tensors, int64_t B,

@@ -31,9 +31,10 @@ constexpr int kMaxHalf = 256;  // D <= 512
 
 struct RopeT {
   const uint16_t* x;
-  uint16_t* out;
+  void* out;  // bf16, or fp32 with of32
   int H;
-  int64_t xsb, xss, xsh, osb, oss, osh;
+  int64_t xsb, xss, xsh, osb, oss, osh;  // elements of x's / out's type
+  int of32;
 };
 
 struct RopeP {
@@ -61,9 +62,9 @@ __device__ __forceinline__ int64_t load_pos(const RopeP& p, int64_t b, int64_t s
 }
 
 template <bool NEOX>
-__device__ __forceinline__ void rotate(const uint4& a, const uint4& c, const float (&cs)[8],
-                                       const float (&sn)[8], uint4& oa, uint4& oc) {
-  float fa[8], fc[8], ra[8], rc[8];
+__device__ __forceinline__ void rotate_f(const uint4& a, const uint4& c, const float (&cs)[8],
+                                         const float (&sn)[8], float (&ra)[8], float (&rc)[8]) {
+  float fa[8], fc[8];
   unpack8(a, fa);
   unpack8(c, fc);
   if (NEOX) {
@@ -85,11 +86,25 @@ __device__ __forceinline__ void rotate(const uint4& a, const uint4& c, const flo
       rc[2 * i + 1] = re2 * sn[4 + i] + im2 * cs[4 + i];
     }
   }
+}
+
+template <bool NEOX>
+__device__ __forceinline__ void rotate(const uint4& a, const uint4& c, const float (&cs)[8],
+                                       const float (&sn)[8], uint4& oa, uint4& oc) {
+  float ra[8], rc[8];
+  rotate_f<NEOX>(a, c, cs, sn, ra, rc);
   oa = pack8(ra);
   oc = pack8(rc);
 }
 
-template <int LPH, bool NEOX, bool TABLE>
+// 8 fp32 values (32 bytes) to out at element offset `off`.
+__device__ __forceinline__ void store_f32x8(const RopeT& T, int64_t off, const float (&v)[8]) {
+  float4* o = reinterpret_cast<float4*>(static_cast<float*>(T.out) + off);
+  o[0] = make_float4(v[0], v[1], v[2], v[3]);
+  o[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+template <int LPH, bool NEOX, bool TABLE, bool ANYF32>
 __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
   __shared__ float sfreq[kMaxHalf];
   const int half = p.D >> 1;
@@ -150,7 +165,7 @@ __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
     if (ti >= p.nt) break;
     const RopeT& T = p.t[ti];
     const uint16_t* xb = T.x + b * T.xsb + s * T.xss;
-    uint16_t* ob = T.out + b * T.osb + s * T.oss;
+    const int64_t ob = b * T.osb + s * T.oss;
     for (int h0 = hs; h0 < T.H; h0 += HPI * UNR) {
       uint4 va[UNR], vc[UNR];
 #pragma unroll
@@ -165,10 +180,17 @@ __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
       for (int u = 0; u < UNR; ++u) {
         const int h = h0 + u * HPI;
         if (h < T.H) {
-          uint4 ra, rc;
-          rotate<NEOX>(va[u], vc[u], cs, sn, ra, rc);
-          st_global(ob + h * T.osh + oa, ra);
-          st_global(ob + h * T.osh + oc, rc);
+          if (ANYF32 && T.of32) {  // fp32 output: the rotated values unrounded
+            float ra[8], rc[8];
+            rotate_f<NEOX>(va[u], vc[u], cs, sn, ra, rc);
+            store_f32x8(T, ob + h * T.osh + oa, ra);
+            store_f32x8(T, ob + h * T.osh + oc, rc);
+          } else {
+            uint4 ra, rc;
+            rotate<NEOX>(va[u], vc[u], cs, sn, ra, rc);
+            st_global(static_cast<uint16_t*>(T.out) + ob + h * T.osh + oa, ra);
+            st_global(static_cast<uint16_t*>(T.out) + ob + h * T.osh + oc, rc);
+          }
         }
       }
     }
@@ -193,7 +215,7 @@ __global__ void __launch_bounds__(256) rope_generic(const RopeP p) {
     if (ti >= p.nt) break;
     const RopeT& T = p.t[ti];
     const uint16_t* xb = T.x + b * T.xsb + s * T.xss;
-    uint16_t* ob = T.out + b * T.osb + s * T.oss;
+    const int64_t ob = b * T.osb + s * T.oss;
     for (int64_t q = threadIdx.x; q < static_cast<int64_t>(T.H) * half; q += blockDim.x) {
       const int h = static_cast<int>(q / half), jj = static_cast<int>(q - static_cast<int64_t>(h) * half);
       float cv, sv;
@@ -213,29 +235,41 @@ __global__ void __launch_bounds__(256) rope_generic(const RopeP p) {
       const float c = bf16_to_f(xb[h * T.xsh + ic]);
       const float ra = a * cv - c * sv;
       const float rc = NEOX ? c * cv + a * sv : a * sv + c * cv;
-      ob[h * T.osh + ia] = f_to_bf16(ra);
-      ob[h * T.osh + ic] = f_to_bf16(rc);
+      if (T.of32) {
+        static_cast<float*>(T.out)[ob + h * T.osh + ia] = ra;
+        static_cast<float*>(T.out)[ob + h * T.osh + ic] = rc;
+      } else {
+        static_cast<uint16_t*>(T.out)[ob + h * T.osh + ia] = f_to_bf16(ra);
+        static_cast<uint16_t*>(T.out)[ob + h * T.osh + ic] = f_to_bf16(rc);
+      }
     }
   }
 }
 
+template <bool NEOX, bool TABLE, bool ANYF32>
+int launch_rope_vec(const RopeP& p, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(ceil_div(p.B * p.S, 8)));
+  switch (p.D / 16) {
+    case 1: rope_vec<1, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 2: rope_vec<2, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 4: rope_vec<4, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 8: rope_vec<8, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 16: rope_vec<16, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 32: rope_vec<32, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    default: return FRAG_ERR_SHAPE;
+  }
+  return check_launch();
+}
+
 template <bool NEOX, bool TABLE>
 int launch_rope_t(const RopeP& p, bool vec, cudaStream_t s) {
-  const int64_t tokens = p.B * p.S;
   if (vec) {
-    const dim3 grid(static_cast<unsigned>(ceil_div(tokens, 8)));
-    switch (p.D / 16) {
-      case 1: rope_vec<1, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
-      case 2: rope_vec<2, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
-      case 4: rope_vec<4, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
-      case 8: rope_vec<8, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
-      case 16: rope_vec<16, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
-      case 32: rope_vec<32, NEOX, TABLE><<<grid, 256, 0, s>>>(p); break;
-      default: return FRAG_ERR_SHAPE;
-    }
-  } else {
-    rope_generic<NEOX, TABLE><<<dim3(static_cast<unsigned>(tokens)), 256, 0, s>>>(p);
+    // fp32 outputs get their own instantiation: the bf16-only kernel keeps
+    // its register count (and CTAs per SM)
+    const bool anyf32 = p.t[0].of32 || (p.nt > 1 && p.t[1].of32);
+    return anyf32 ? launch_rope_vec<NEOX, TABLE, true>(p, s) : launch_rope_vec<NEOX, TABLE, false>(p, s);
   }
+  rope_generic<NEOX, TABLE><<<dim3(static_cast<unsigned>(p.B * p.S)), 256, 0, s>>>(p);
   return check_launch();
 }
 
@@ -285,14 +319,15 @@ extern "C" int frag_rope(const frag_rope_tensor* tensors, int num_tensors, int64
 
   bool vec = D % 16 == 0 && (D / 16) <= 32 && (32 % (D / 16)) == 0;
   if (freqs) vec = vec && aligned16(freqs) && freqs_stride % 2 == 0;
-  p.t[1] = RopeT{nullptr, nullptr, 0, 0, 0, 0, 0, 0, 0};
+  p.t[1] = RopeT{nullptr, nullptr, 0, 0, 0, 0, 0, 0, 0, 0};
   for (int i = 0; i < num_tensors; ++i) {
     const frag_rope_tensor& t = tensors[i];
     if (t.H < 0 || t.H > 0x7fffffffLL) return FRAG_ERR_SHAPE;
     if (t.H > 0 && (!t.x || !t.out)) return FRAG_ERR_INVALID_ARG;
-    p.t[i] = RopeT{static_cast<const uint16_t*>(t.x), static_cast<uint16_t*>(t.out),
-                   static_cast<int>(t.H), t.x_stride_b, t.x_stride_s, t.x_stride_h,
-                   t.out_stride_b, t.out_stride_s, t.out_stride_h};
+    if (t.out_dtype != FRAG_ROPE_OUT_BF16 && t.out_dtype != FRAG_ROPE_OUT_F32) return FRAG_ERR_INVALID_ARG;
+    p.t[i] = RopeT{static_cast<const uint16_t*>(t.x), t.out, static_cast<int>(t.H), t.x_stride_b,
+                   t.x_stride_s, t.x_stride_h, t.out_stride_b, t.out_stride_s, t.out_stride_h,
+                   t.out_dtype == FRAG_ROPE_OUT_F32 ? 1 : 0};
     const int64_t st[6] = {t.x_stride_b, t.x_stride_s, t.x_stride_h,
                            t.out_stride_b, t.out_stride_s, t.out_stride_h};
     for (int k = 0; k < 6; ++k) vec = vec && (st[k] % 8 == 0);

@@ -454,9 +454,12 @@ def _rope_desc(x: torch.Tensor, out: torch.Tensor, name: str) -> _lib.RopeTensor
         raise ValueError(f"{name}: the head dimension must be contiguous")
     if out.shape != x.shape:
         raise ValueError(f"{name}: output shape {tuple(out.shape)} != {tuple(x.shape)}")
+    if out.dtype not in (torch.bfloat16, torch.float32) or out.device != x.device:
+        raise TypeError(f"{name}: the output must be bf16 or float32 on {x.device}")
     B, S, H, D = x.shape
+    odt = _lib.FRAG_ROPE_OUT_F32 if out.dtype == torch.float32 else _lib.FRAG_ROPE_OUT_BF16
     return _lib.RopeTensor(x.data_ptr(), out.data_ptr(), H, x.stride(0), x.stride(1), x.stride(2),
-                           out.stride(0), out.stride(1), out.stride(2))
+                           out.stride(0), out.stride(1), out.stride(2), odt)
 
 
 def _new_out(x: torch.Tensor, out_layout: str) -> torch.Tensor:
@@ -483,7 +486,8 @@ def rope(q: torch.Tensor, k: torch.Tensor | None = None, positions: torch.Tensor
     backward).  out_layout="bhsd" writes new outputs in the [B, H, S, D]
     storage order attention kernels read (the transpose is fused into the
     stores; the returned tensors are [B, S, H, D] views of that storage, so
-    `.transpose(1, 2)` gives contiguous [B, H, S, D])."""
+    `.transpose(1, 2)` gives contiguous [B, H, S, D]).  An out_q / out_k of
+    dtype float32 receives the rotated values unrounded."""
     _need(q, "q", torch.bfloat16)
     dev = q.device
     if layout not in _LAYOUTS:

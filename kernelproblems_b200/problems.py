@@ -15,9 +15,8 @@ Errors are Python exceptions (TypeError/ValueError for bad inputs, FragError
 for a failed launch), as the reference harness expects.  Inputs are never
 modified; outputs are new tensors on the inputs' device.
 
-Problems whose graphs are outside the library's ops are not registered:
-v7/0f38bc55457c returns q in fp32, and v8/43f0c930291e, v8/7e38211c7f1c are
-broken in the reference itself (their inputs do not match their graphs).  v8/f6251e84e3fa is broken the same way
+Problems not registered: v8/43f0c930291e and v8/7e38211c7f1c are broken in
+the reference itself (their inputs do not match their graphs).  v8/f6251e84e3fa is broken the same way
 (its first input should be the (y, rstd) pair of a _fused_rms_norm); its
 drop-in is registered and works when given that pair.
 """
@@ -187,6 +186,17 @@ def rope_c8c60d8f7015(arg586_1, arg582_1, mm, mm_1):
                     layout="interleaved")
 
 
+def rope_f32q_0f38bc55457c(mm, mm_1, arg586_1, arg582_1):
+    """v7/0f38bc55457c/optimized_kernel.py:84: as c8c60d8f7015, but q is
+    returned in fp32 (the graph never rounds it back to bf16) ->
+    (q fp32 [1,S,32,128], k bf16 [1,S,8,128])."""
+    S = mm.shape[0]
+    qv = _heads(mm, S)
+    oq = torch.empty(qv.shape, dtype=torch.float32, device=mm.device)
+    return ops.rope(qv, _heads(mm_1, S), arg586_1.view(1, S), freqs=arg582_1,
+                    layout="interleaved", out_q=oq)
+
+
 def rope_97032595d968(mm, mm_1, arg586_1, arg582_1):
     """v8/97032595d968/optimized_kernel.py:44: as c8c60d8f7015, argument order
     (mm, mm_1, positions, freqs)."""
@@ -341,6 +351,7 @@ PROBLEMS: dict[str, Callable] = {
     "v7/a12a160cb11b": emb_bwd_a12a160cb11b,
     "v8/c8c60d8f7015": rope_c8c60d8f7015,
     "v6/c8c60d8f7015": rope_c8c60d8f7015,
+    "v7/0f38bc55457c": rope_f32q_0f38bc55457c,
     "v8/97032595d968": rope_97032595d968,
     "v6/97032595d968": rope_97032595d968,
     "v8/493cad38cac9": rope_493cad38cac9,

@@ -125,6 +125,19 @@ def rope_c8c60d8f7015(pos, freqs, mm, mm_1):
     return (_rope_rows(mm, 8192, f), _rope_rows(mm_1, 8192, f))
 
 
+def rope_f32q_0f38bc55457c(mm, mm_1, pos, freqs):
+    """v7/0f38bc55457c/problem.py:10-40: the complex-pair RoPE of
+    c8c60d8f7015 with q left in fp32 (only k is cast back to bf16)."""
+    f = aten.view.default(aten.index.Tensor(freqs, [aten.squeeze.dim(pos, 0)]), [1, 8192, 1, 64])
+    out = []
+    for t, h in ((mm, 32), (mm_1, 8)):
+        x = aten._to_copy.default(aten.view.default(aten._unsafe_view.default(t, [1, 8192, h * 128]),
+                                                    [1, 8192, -1, 128]), dtype=torch.float32)
+        xc = aten.view_as_complex.default(aten.view.default(x, [1, 8192, h, -1, 2]))
+        out.append(aten.view.default(aten.view_as_real.default(aten.mul.Tensor(xc, f)), [1, 8192, h, 128]))
+    return (out[0], aten._to_copy.default(out[1], dtype=torch.bfloat16))
+
+
 def rope_97032595d968(mm, mm_1, pos, freqs):
     """v8/97032595d968/problem.py (same graph, argument order mm, mm_1, pos, freqs)."""
     return rope_c8c60d8f7015(pos, freqs, mm, mm_1)
@@ -252,6 +265,7 @@ ORACLES = {
     "v7/a12a160cb11b": emb_bwd_a12a160cb11b,
     "v8/c8c60d8f7015": rope_c8c60d8f7015,
     "v6/c8c60d8f7015": rope_c8c60d8f7015,
+    "v7/0f38bc55457c": rope_f32q_0f38bc55457c,
     "v8/97032595d968": rope_97032595d968,
     "v6/97032595d968": rope_97032595d968,
     "v8/493cad38cac9": rope_493cad38cac9,

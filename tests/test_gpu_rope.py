@@ -84,3 +84,24 @@ def test_rope_in_place():
     xd = x.to(DEV)
     ops.rope(xd, None, pos.to(DEV), theta=500000.0, out_q=xd)
     assert_bf16_close(xd, ora.rope_neox(x, pos, 500000.0), "in place")
+
+
+@pytest.mark.parametrize("D", [128, 6])
+def test_rope_fp32_output_is_unrounded(D):
+    """out_q in float32 (v7/0f38bc55457c returns q that way): the rotated
+    values of the bf16 input, not rounded; k still bf16."""
+    from conftest import assert_f32_close
+    S, Hq, Hk = 32, 4, 2
+    g = torch.Generator().manual_seed(31)
+    q = torch.randn(1, S, Hq, D, generator=g).bfloat16()
+    k = torch.randn(1, S, Hk, D, generator=g).bfloat16()
+    freqs = torch.randn(64, D // 2, generator=g, dtype=torch.complex64)
+    pos = torch.randint(0, 64, (1, S), generator=g, dtype=torch.int32)
+    oq = torch.empty(1, S, Hq, D, dtype=torch.float32, device="cuda")
+    oq, ok = ops.rope(q.cuda(), k.cuda(), pos.cuda(), freqs=freqs.cuda(), layout="interleaved",
+                      out_q=oq)
+    f = freqs[pos[0].long()].view(1, S, 1, D // 2)
+    ref_q = torch.view_as_real(torch.view_as_complex(q.float().reshape(1, S, Hq, -1, 2)) * f).reshape(q.shape)
+    assert oq.dtype == torch.float32 and ok.dtype == torch.bfloat16
+    assert_f32_close(oq.cpu(), ref_q, "fp32 q", rtol=1e-5, atol=1e-5)
+    assert_bf16_close(ok.cpu(), ora.rope_interleaved(k, f), "bf16 k")
