@@ -15,8 +15,11 @@ Errors are Python exceptions (TypeError/ValueError for bad inputs, FragError
 for a failed launch), as the reference harness expects.  Inputs are never
 modified; outputs are new tensors on the inputs' device.
 
-Problems not registered: v8/43f0c930291e and v8/7e38211c7f1c are broken in
-the reference itself (their inputs do not match their graphs).  v8/f6251e84e3fa is broken the same way
+Three problems are broken in the reference itself: v8/f6251e84e3fa,
+v8/43f0c930291e and v8/7e38211c7f1c pass a 0-d tensor where their graphs
+index a tuple.  Their drop-ins are registered: they work when given the tuple
+the graph expects, and raise IndexError on the reference's own inputs, as the
+reference Model does.  v8/f6251e84e3fa is broken the same way
 (its first input should be the (y, rstd) pair of a _fused_rms_norm); its
 drop-in is registered and works when given that pair.
 """
@@ -137,6 +140,25 @@ def add_rms_bwd_d8f596b3df34(mm_664, mm_666, add_recomputed, getitem_12_recomput
     return dres.view(-1, N), dw
 
 
+def add3_rms_bwd_43f0c930291e(_fused_rms_norm_2_recomputed, mm_656, mm_658, mm_660, add_1,
+                              _unsafe_view_450, add_215):
+    """v8/43f0c930291e/problem.py:10-38: dy = mm_656 + mm_658 + mm_660 (each
+    partial sum bf16), backward against add_1 with the saved rstd
+    _fused_rms_norm_2_recomputed[1], d_res = add_215 + dx ->
+    (d_res [M, N], dweight fp32).  The reference's own get_inputs passes a 0-d
+    tensor as the (y, rstd) pair (indexing it raises IndexError, as the
+    reference Model does)."""
+    rstd = _fused_rms_norm_2_recomputed[1]
+    x = add_1.contiguous()
+    N = x.shape[-1]
+    dres, dw = ops.rmsnorm_bwd(mm_656.contiguous().view(x.shape), x,
+                               rstd.contiguous().view(x.shape[:-1]), _unsafe_view_450,
+                               dy2=mm_658.contiguous().view(x.shape),
+                               dy3=mm_660.contiguous().view(x.shape),
+                               dres=add_215.contiguous(), dw_dtype=torch.float32)
+    return dres.view(-1, N), dw
+
+
 def add3_rms_bwd_ed20955ec34b(mm_672, view_1794, mm_674, embedding, getitem_1_recomputed,
                               _unsafe_view_432, add_220):
     """v7/ed20955ec34b/optimized_kernel.py:118: dy = view_1794 + mm_672 + mm_674
@@ -233,6 +255,14 @@ def rope_bwd_bfe872e373e4(getitem_641, clone_63):
     """v7/bfe872e373e4/optimized_kernel.py:54: q-grad [1,32,S,128] strided view
     times clone_63 (already conjugated upstream) -> [S, 4096]."""
     return _rope_bwd_strided(getitem_641, clone_63)
+
+
+def rope_bwd_7e38211c7f1c(_scaled_dot_product_flash_attention_backward_31, clone_62):
+    """v8/7e38211c7f1c/problem.py:10-31: the k-gradient is entry [1] of the
+    SDPA backward's outputs ([1, 8, S, 128], a transposed view) -> [S, 1024].
+    The reference's own get_inputs passes a 0-d tensor there (indexing it
+    raises IndexError, as the reference Model does)."""
+    return _rope_bwd_strided(_scaled_dot_product_flash_attention_backward_31[1], clone_62)
 
 
 def rope_bwd_5c65f62b0422(getitem_642, clone_62):
@@ -344,6 +374,7 @@ PROBLEMS: dict[str, Callable] = {
     "v7/7f544ceb2120": add_rms_bwd_7f544ceb2120,
     "v8/d8f596b3df34": add_rms_bwd_d8f596b3df34,
     "v7/ed20955ec34b": add3_rms_bwd_ed20955ec34b,
+    "v8/43f0c930291e": add3_rms_bwd_43f0c930291e,
     "v7/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v6/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v5/1e49beb8a123": emb_fwd_1e49beb8a123,
@@ -360,6 +391,7 @@ PROBLEMS: dict[str, Callable] = {
     "v7/e29b92927600": rope_e29b92927600,
     "v7/bfe872e373e4": rope_bwd_bfe872e373e4,
     "v7/5c65f62b0422": rope_bwd_5c65f62b0422,
+    "v8/7e38211c7f1c": rope_bwd_7e38211c7f1c,
     "v6/03d64c25b654": rope_bwd_03d64c25b654,
 }
 

@@ -96,6 +96,16 @@ def add_rms_bwd_d8f596b3df34(mm_664, mm_666, h, rstd, w, add_218):
     return (out.view(8192, 4096), aten._to_copy.default(dw, dtype=torch.float32))
 
 
+def add3_rms_bwd_43f0c930291e(recomputed, mm_656, mm_658, mm_660, add_1, w, add_215):
+    """v8/43f0c930291e/problem.py:10-38: rstd = recomputed[1], dy = add(add(mm_656,
+    mm_658), mm_660), d_res viewed [8192, 4096]."""
+    dy = aten.add.Tensor(aten.view.default(mm_656, [1, 8192, 4096]), aten.view.default(mm_658, [1, 8192, 4096]))
+    dy = aten.add.Tensor(dy, aten.view.default(mm_660, [1, 8192, 4096]))
+    dx, dw = F.rmsnorm_bwd(dy, add_1, recomputed[1], w)
+    out = aten.add.Tensor(add_215, dx)
+    return (aten.view.default(out, [8192, 4096]), aten._to_copy.default(dw, dtype=torch.float32))
+
+
 def add3_rms_bwd_ed20955ec34b(mm_672, view_1794, mm_674, embedding, rstd, w, add_220):
     """v7/ed20955ec34b/problem.py:19-44: dy = add(add(view_1794, mm_672), mm_674)."""
     dy = aten.add.Tensor(view_1794, aten.view.default(mm_672, [1, 8192, 4096]))
@@ -163,6 +173,12 @@ def _rope_bwd(grad_bhsd, freqs):
 def rope_bwd_bfe872e373e4(g, freqs):
     """v7/bfe872e373e4/problem.py:17-34."""
     return _rope_bwd(g, freqs)
+
+
+def rope_bwd_7e38211c7f1c(sdpa_bwd_out, freqs):
+    """v8/7e38211c7f1c/problem.py:10-31: entry [1] of the SDPA backward's
+    outputs, then the same multiply as 5c65f62b0422."""
+    return _rope_bwd(sdpa_bwd_out[1], freqs)
 
 
 def rope_bwd_5c65f62b0422(g, freqs):
@@ -258,6 +274,7 @@ ORACLES = {
     "v7/7f544ceb2120": add_rms_bwd_7f544ceb2120,
     "v8/d8f596b3df34": add_rms_bwd_d8f596b3df34,
     "v7/ed20955ec34b": add3_rms_bwd_ed20955ec34b,
+    "v8/43f0c930291e": add3_rms_bwd_43f0c930291e,
     "v7/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v6/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v5/1e49beb8a123": emb_fwd_1e49beb8a123,
@@ -274,5 +291,6 @@ ORACLES = {
     "v7/e29b92927600": rope_e29b92927600,
     "v7/bfe872e373e4": rope_bwd_bfe872e373e4,
     "v7/5c65f62b0422": rope_bwd_5c65f62b0422,
+    "v8/7e38211c7f1c": rope_bwd_7e38211c7f1c,
     "v6/03d64c25b654": rope_bwd_03d64c25b654,
 }

@@ -45,15 +45,21 @@ def make_input(spec: dict, device="cpu") -> torch.Tensor:
     return base.as_strided(tuple(v["shape"]), tuple(v["stride"]), int(v["offset"]))
 
 
-# Inputs computed from other inputs of the same problem (see make_golden.py's
-# INPUT_FIXUPS): "fused_rms_norm" is the (y, rstd) pair that
-# aten._fused_rms_norm(inputs[x], [N], inputs[w], eps) returns on the CPU.
-DERIVED = ("fused_rms_norm",)
+# Inputs rebuilt for problems whose own get_inputs() does not match their
+# graph (see make_golden.py's INPUT_FIXUPS):
+#   "fused_rms_norm": the (y, rstd) pair that
+#     aten._fused_rms_norm(inputs[x], [N], inputs[w], eps) returns on the CPU;
+#   "tuple_slot": a tuple of `len` entries whose entry `slot` is the tensor
+#     described by `item` (a seeded spec like any other input), the rest None.
+DERIVED = ("fused_rms_norm", "tuple_slot")
 
 
 def make_inputs(specs: list[dict], device="cpu") -> list:
     out = [None if s["kind"] in DERIVED else make_input(s, device) for s in specs]
     for i, s in enumerate(specs):
+        if s["kind"] == "tuple_slot":
+            item = make_input(s["item"], device)
+            out[i] = tuple(item if j == s["slot"] else None for j in range(s["len"]))
         if s["kind"] == "fused_rms_norm":
             x, w = out[s["x"]].cpu(), out[s["w"]].cpu()
             y, rstd = torch.ops.aten._fused_rms_norm.default(x, [w.numel()], w, float(s["eps"]))

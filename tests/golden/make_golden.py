@@ -42,8 +42,20 @@ SEED_BASE = 20260
 # so the reference FAILs with "index 1 is out of bounds" (benchmark.json).
 # The graph wants the (y, rstd) pair of _fused_rms_norm over its own
 # `embedding` (input 4) and weight (input 5) at eps 1e-5.
+# v8/43f0c930291e: the same, with add_1 (input 4) and the weight (input 5).
+# v8/7e38211c7f1c: get_inputs passes torch.randn([]) as the output tuple of
+# _scaled_dot_product_flash_attention_backward, whose entry [1] the graph uses
+# as bf16 [1, 8, 8192, 128] with strides (8388608, 128, 1024, 1), a
+# transposed view of [8192, 8, 128] storage (problem.py:16); the tuple is
+# rebuilt with a seeded tensor of exactly that layout in that slot.
 INPUT_FIXUPS = {
     "v8/f6251e84e3fa": {0: {"kind": "fused_rms_norm", "x": 4, "w": 5, "eps": 1e-5}},
+    "v8/43f0c930291e": {0: {"kind": "fused_rms_norm", "x": 4, "w": 5, "eps": 1e-5}},
+    "v8/7e38211c7f1c": {0: {"kind": "tuple_slot", "slot": 1, "len": 3,
+                            "item": {"kind": "randn", "size": [8192, 8, 128], "dtype": "bfloat16",
+                                     "seed": 7_938_211,
+                                     "view": {"shape": [1, 8, 8192, 128],
+                                              "stride": [8388608, 128, 1024, 1], "offset": 0}}}},
 }
 
 

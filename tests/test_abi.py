@@ -79,11 +79,13 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     _lib.load()
 
 
-def test_broken_reference_input_fails_like_the_reference():
-    """v8/f6251e84e3fa's own get_inputs passes a 0-d tensor where the graph
-    indexes [1] of the (y, rstd) pair; the reference Model raises IndexError
-    there, and so does the drop-in (before touching the GPU)."""
+@pytest.mark.parametrize("key,n_inputs", [("v8/f6251e84e3fa", 8), ("v8/43f0c930291e", 7),
+                                          ("v8/7e38211c7f1c", 2)])
+def test_broken_reference_input_fails_like_the_reference(key, n_inputs):
+    """These problems' own get_inputs pass a 0-d tensor where the graph
+    indexes [1] of a tuple; the reference Model raises IndexError there, and
+    so does the drop-in (before touching the GPU)."""
     import torch
     from kernelproblems_b200.problems import PROBLEMS
     with pytest.raises(IndexError):
-        PROBLEMS["v8/f6251e84e3fa"](torch.randn([]), *[None] * 7)
+        PROBLEMS[key](torch.randn([]), *[None] * (n_inputs - 1))

@@ -29,7 +29,8 @@ pytestmark = pytest.mark.gpu
 FIXTURES = sorted(GOLDEN.glob("v*_*.pt"))
 
 EXACT = {"v7/1e49beb8a123", "v6/1e49beb8a123", "v5/1e49beb8a123", "v4/1e49beb8a123"}
-RMS_BWD = {"v7/45990c83cfd6", "v7/7f544ceb2120", "v8/d8f596b3df34", "v7/ed20955ec34b"}
+RMS_BWD = {"v7/45990c83cfd6", "v7/7f544ceb2120", "v8/d8f596b3df34", "v7/ed20955ec34b",
+           "v8/43f0c930291e"}
 EMB_BWD = {"v7/a12a160cb11b"}
 UNSHARD = {"v8/8e33a91b7364", "v7/8e33a91b7364", "v6/8e33a91b7364"}  # output 1: a copy
 # norm -> embedding backward chain: output index of (dweight, table gradient)
@@ -68,6 +69,11 @@ def _dw_f64(key, cpu_in):
         x, w, dy = cpu_in
         _, rstd = F.rmsnorm_fwd(x, w, 1e-5)
         return F.rmsnorm_dw_f64(dy, x, rstd), (dy, x, rstd)
+    if key == "v8/43f0c930291e":
+        rec, mm_656, mm_658, mm_660, h, w, _ = cpu_in
+        dy = torch.ops.aten.add.Tensor(mm_656.view(h.shape), mm_658.view(h.shape))
+        dy = torch.ops.aten.add.Tensor(dy, mm_660.view(h.shape))
+        return F.rmsnorm_dw_f64(dy, h, rec[1]), (dy, h, rec[1])
     if key == "v7/ed20955ec34b":
         mm_672, view_1794, mm_674, h, rstd, w, _ = cpu_in
         dy = torch.ops.aten.add.Tensor(view_1794, mm_672.view(h.shape))
