@@ -51,10 +51,14 @@ NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 SUITE = ["C0F", "C2F", "C1B", "C3F", "C2B", "C3B", "C4F", "C4B"]
 DOMINANT = "C4B"  # largest share of the step; its main kernel is the roofline kernel
-# Fusions beyond the five configurations (SURVEY "next" rows), measured on request:
+# Fusions and callers beyond the five configurations, measured on request:
 #   C2N  embedding gather + RMSNorm fused (C2 ids/table, eps 1e-5)
 #   C3S  RoPE fwd writing q/k in the [B, H, S, D] layout attention reads (C3 shapes)
-NEXT = ["C2N", "C3S", "C2C", "C2U", "C2S"]
+#   C2C  RMSNorm bwd -> embedding bwd chain fused (C2U: the same unfused)
+#   C2S  FSDP table unshard + add/RMSNorm (one grouped copy, then the norm)
+#   C2L  FSDP decoder-layer unshard (8 splits) + add/RMSNorm
+#   C1R  RMSNorm forward recomputed in its backward, one pass (C1U: two calls)
+NEXT = ["C2N", "C3S", "C2C", "C2U", "C2S", "C2L", "C1R", "C1U"]
 
 
 # ------------------------------------------------------------------ helpers
@@ -126,10 +130,30 @@ class ClockSampler:
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        # sampling is running before the timed region starts (a short region
+        # would otherwise end before nvidia-smi's first sample)
+        self._wait_lines(1, 5.0)
+
+    def _lines(self) -> int:
+        try:
+            return len(Path(self.path).read_text().splitlines())
+        except OSError:
+            return 0
+
+    def _wait_lines(self, n: int, limit_s: float) -> None:
+        t_end = time.monotonic() + limit_s
+        while self._lines() < n and time.monotonic() < t_end and self.proc.poll() is None:
+            time.sleep(0.01)
+
+    def start(self):
+        """Mark the start of the timed region: stop() waits for a sample after it."""
+        self.n0 = self._lines() if self.proc is not None else 0
 
     def stop(self):
         if self.proc is None:
             return None
+        self._wait_lines(getattr(self, "n0", 0) + 1, 1.0)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -507,32 +531,71 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
         f.e2e = lambda h: _e2e_call(lambda xs: unfused(**xs), h)
         return f
 
-    def mk_c2s():
-        # FSDP unshard of the embedding table out of the all-gather buffer plus
-        # the final add + RMSNorm with the gathered weight, at the shapes of
-        # the reference problem (v8/8e33a91b7364: buffer [525340672] viewed
-        # [8, -1], splits [512, 65667072], rows [8192, 4096])
+    def mk_fwd_bwd(tag):
+        # RMSNorm forward recomputed in its backward at the shapes of
+        # v6/822931829090 (x [8192, 4096], dy = mm_656 + mm_658 + mm_660,
+        # dres, y returned): one frag_rmsnorm_fwd_bwd pass (C1R), or the
+        # forward and the backward as two calls (C1U)
+        M, N = 8192, 4096
+        w = cf.rmsnorm_weight(N, device=dev, seed=seed0 + 50)
+        x = cf.randn((1, M, N), device=dev, seed=seed0 + 51)
+        dys = [cf.randn((1, M, N), device=dev, seed=seed0 + 52 + i) for i in range(3)]
+        dres = cf.randn((1, M, N), device=dev, seed=seed0 + 55)
+        ws = torch.empty(ops.rmsnorm_bwd_workspace_bytes(M, N), dtype=torch.uint8, device=dev)
+
+        def fused(x, d0, d1, d2, dres):
+            return ops.rmsnorm_fwd_bwd(x, w, d0, dy2=d1, dy3=d2, dres=dres, eps=1e-5, workspace=ws)
+
+        def unfused(x, d0, d1, d2, dres):
+            y, r = ops.rmsnorm_fwd(x, w, 1e-5)
+            dx, dw = ops.rmsnorm_bwd(d0, x, r, w, dy2=d1, dy3=d2, dres=dres, eps=1e-5, workspace=ws)
+            return y, dx, dw
+        fn = fused if tag == "C1R" else unfused
+        label = ("RMSNorm fwd recomputed in bwd [8192,4096], 3 grads + dres, "
+                 + ("fused" if tag == "C1R" else "fwd then bwd"))
+        f = Frag(tag, label, M, cf.bytes_rmsnorm_fwd_bwd(M, N, 1, 3, True, True),
+                 [("rmsnorm_fwd_bwd" if tag == "C1R" else "rmsnorm_fwd+bwd",
+                   lambda: fn(x, *dys, dres))])
+        f.host = dict(x=x, d0=dys[0], d1=dys[1], d2=dys[2], dres=dres)
+        f.e2e = lambda h: _e2e_call(lambda xs: fn(**xs), h)
+        return f
+
+    def mk_unshard(tag, splits, ncopy, label):
+        # FSDP unshard of parameters out of one all-gather buffer viewed
+        # [8, -1] (split 0 the norm weight) in one grouped copy, plus the add
+        # + RMSNorm with the gathered weight, at the reference's shapes
         M, N, W = 8192, 4096, 8
-        shard = 65667072
         res = cf.randn((1, M, N), device=dev, seed=seed0 + 40)
         x = cf.randn((M, N), device=dev, seed=seed0 + 41)
-        flat = cf.randn((W * (512 + shard),), device=dev, seed=seed0 + 42).view(W, -1)
-        table = torch.empty(W, shard, dtype=torch.bfloat16, device=dev)
+        flat = cf.randn((W * sum(splits),), device=dev, seed=seed0 + 42)
+        outs = [torch.empty(W, n, dtype=torch.bfloat16, device=dev) for n in splits[:ncopy]]
         y = torch.empty_like(res)
 
-        def step(res, x, flat, out=None, y=None):
-            w = ops.copy_rows(flat[:, :512]).view(-1)
-            _, yy, _ = ops.add_rmsnorm_fwd(res, x.view(res.shape), w, 1e-5, write_h=False,
-                                           save_rstd=False, y_out=y)
-            return yy, ops.copy_rows(flat[:, 512:], out=out)
-        f = Frag("C2S", "FSDP table unshard + add/RMSNorm [8192,4096] (8 shards of 65667072)", M,
-                 cf.bytes_add_rmsnorm_unshard(M, N, W, shard),
-                 [("unshard_add_rmsnorm", lambda: step(res, x, flat, out=table, y=y))])
+        def step(res, x, flat, outs=None, y=None):
+            parts = ops.copy_rows_grouped(torch.split(flat.view(W, -1), splits, dim=1)[:ncopy], outs)
+            _, yy, _ = ops.add_rmsnorm_fwd(res, x.view(res.shape), parts[0].view(-1), 1e-5,
+                                           write_h=False, save_rstd=False, y_out=y)
+            return yy, parts
+        f = Frag(tag, label, M, cf.bytes_add_rmsnorm_unshard(M, N, W, sum(splits[1:ncopy])),
+                 [("unshard_add_rmsnorm", lambda: step(res, x, flat, outs=outs, y=y))])
         f.host = dict(res=res, x=x, flat=flat)
         f.e2e = lambda h: _e2e_call(lambda xs: step(xs["res"], xs["x"], xs["flat"]), h)
         return f
 
-    builders = {"C2N": mk_c2n, "C3S": mk_c3s, "C2S": mk_c2s, "C2C": lambda: mk_chain("C2C"),
+    def mk_c2s():
+        # v8/8e33a91b7364: buffer [525340672], splits [512, 65667072]
+        return mk_unshard("C2S", [512, 65667072], 2,
+                          "FSDP table unshard + add/RMSNorm [8192,4096] (8 shards of 65667072)")
+
+    def mk_c2l():
+        # v8/7815074de963: one decoder layer's buffer [218112000], splits
+        # [512, 2097152, 524288, 524288, 2097152, 512, 7340032 x3], 0-7 copied
+        sp = [512, 2097152, 524288, 524288, 2097152, 512, 7340032, 7340032, 7340032]
+        return mk_unshard("C2L", sp, 8,
+                          "FSDP layer unshard (8 splits) + add/RMSNorm [8192,4096]")
+
+    builders = {"C2N": mk_c2n, "C3S": mk_c3s, "C2S": mk_c2s, "C2L": mk_c2l,
+                "C1R": lambda: mk_fwd_bwd("C1R"), "C1U": lambda: mk_fwd_bwd("C1U"), "C2C": lambda: mk_chain("C2C"),
                 "C2U": lambda: mk_chain("C2U"), "C0F": mk_c0f, "C1B": lambda: mk_rms_bwd("C1B", C1, False, 3, False),
                 "C2F": lambda: mk_c2("C2F"), "C2B": lambda: mk_c2("C2B"),
                 "C3F": lambda: mk_c3("C3F"), "C3B": lambda: mk_c3("C3B"),
@@ -692,13 +755,18 @@ def cpu_baseline(names, target_s: float):
 
 # ---------------------------------------------------------------- main arms
 
-def config_dict(workload, world, l2_note):
+def suite_descriptions(names, other: dict | None = None) -> dict:
+    """Config name of each suite fragment (both arms report the same), the
+    given description of any other."""
     from kernelproblems_b200 import configs as cf
-    return {"workload": workload,
-            "fragments": {"C0F": cf.C0.name, "C1B": cf.C1.name, "C2F": cf.C2.name + " fwd",
-                          "C2B": cf.C2.name + " bwd fp32 table", "C3F": cf.C3.name + " fwd",
-                          "C3B": cf.C3.name + " bwd", "C4F": cf.C4.name + " fwd",
-                          "C4B": cf.C4.name + " bwd"},
+    desc = {"C0F": cf.C0.name, "C1B": cf.C1.name, "C2F": cf.C2.name + " fwd",
+            "C2B": cf.C2.name + " bwd fp32 table", "C3F": cf.C3.name + " fwd",
+            "C3B": cf.C3.name + " bwd", "C4F": cf.C4.name + " fwd", "C4B": cf.C4.name + " bwd"}
+    return {n: desc.get(n, (other or {}).get(n, n)) for n in names}
+
+
+def config_dict(workload, world, l2_note, fragments: dict):
+    return {"workload": workload, "fragments": fragments,
             "parallelism": f"dp{world} (rows per rank fixed; dweight exchange for C1B/C4B)",
             "l2": l2_note}
 
@@ -726,7 +794,7 @@ def reference_arm(args, rank, world):
             "n_gpus": world, "steps": steps, "warmup": warm,
             "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-            "config": config_dict(args.workload, 1, "n/a (CPU)"),
+            "config": config_dict(args.workload, 1, "n/a (CPU)", suite_descriptions(names)),
             "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": torch.get_num_threads(),
                              "kind": "port",
                              "sample": (f"torch-eager CPU restatement of the reference graphs "
@@ -764,6 +832,7 @@ def ours_arm(args, rank, local_rank, world):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    clocks.start()
     t_start.record(stream)
     for _ in range(K):
         step.run()
@@ -832,7 +901,10 @@ def ours_arm(args, rank, local_rank, world):
             "data": "synthetic (seeded generators with the configs' shapes and distributions)",
             "config": config_dict(args.workload, world,
                                   "inputs larger than L2 across a step: each fragment's inputs were last "
-                                  "touched one step (>17 GB of traffic) earlier; no explicit flush"),
+                                  f"touched one step ({step_bytes / 1e9:.2f} GB of traffic, L2 0.126 GB) "
+                                  "earlier; no explicit flush",
+                                  suite_descriptions([f.name for f in frags],
+                                                     {f.name: f.desc for f in frags})),
             "pct_of_8TBs_per_gpu": round(100 * value / world / NOMINAL_HBM_GBS, 1),
             "frac_of_measured_per_gpu": round(value / world / peak, 3),
             "tokens_per_s_sum_over_fragments": round(world * tokens / (ms_step * 1e-3)),

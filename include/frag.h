@@ -138,6 +138,31 @@ FRAG_API int frag_rmsnorm_bwd3(const void* dy, const void* dy2, const void* dy3,
                                float eps, void* workspace, size_t workspace_bytes,
                                frag_stream_t stream);
 
+/* ------------------------------------------------------------------------- *
+ * RMSNorm forward recomputed inside its backward (activation checkpointing),
+ * one pass over the rows:
+ *   h    = bf16(bf16(x + x2) + x3)          x2, x3 optional (x3 requires x2)
+ *   rstd = 1/sqrt(mean(h^2) + eps)          stored to rstd_out [M] if non-NULL
+ *   y    = bf16((h * rstd) * w)             stored to y_out [M, N] if non-NULL
+ *   g    = bf16(bf16(dy + dy2) + dy3)       dy2, dy3 optional (dy3 requires dy2)
+ *   dx_out = bf16(dres + bf16(dh))          dh the RMSNorm backward of g at (h, rstd)
+ *   dw / dw_bf16 = sum_rows(g * h * rstd)   as frag_rmsnorm_bwd
+ * h is never written.  Same workspace (frag_rmsnorm_bwd_workspace_bytes) and
+ * dweight order as frag_rmsnorm_bwd.  Replaces the _fused_rms_norm ->
+ * [add ->] _fused_rms_norm_backward -> [add ->] _to_copy regions:
+ *   v6/822931829090/problem.py:19-66 (x; dy + dy2 + dy3; dres; y returned),
+ *   v6/e9198b707240/problem.py:18-56 (dy + dy2; dres; y returned),
+ *   v6/408ac0979ac5/problem.py:19-63 (h = x + x2; dy + dy2; dres; y returned),
+ *   v6/28b45679fca1/problem.py:17-41 (h = x + x2; dy),
+ *   v8/3c6c589cdf81/problem.py:18-53 (h = (x + x2) + x3; dy),
+ * and their other snapshots (v1-v5).
+ * ------------------------------------------------------------------------- */
+FRAG_API int frag_rmsnorm_fwd_bwd(const void* x, const void* x2, const void* x3, const void* w,
+                                  const void* dy, const void* dy2, const void* dy3,
+                                  const void* dres, void* y_out, float* rstd_out, void* dx_out,
+                                  float* dw, void* dw_bf16, int64_t M, int64_t N, float eps,
+                                  void* workspace, size_t workspace_bytes, frag_stream_t stream);
+
 /* Row-block count G of frag_rmsnorm_bwd for 16-byte aligned operands.  After
  * a frag_rmsnorm_bwd call the first G*N floats of its workspace hold the
  * per-block dweight partials [G, N] (whether or not dw was requested), which
@@ -277,6 +302,33 @@ FRAG_API int frag_rmsnorm_embedding_bwd(const void* x, const void* w, const floa
  * ------------------------------------------------------------------------- */
 FRAG_API int frag_copy_rows(const void* src, int64_t src_stride, void* dst, int64_t dst_stride,
                             int64_t rows, int64_t row_bytes, frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Grouped row-strided copy: up to FRAG_COPY_MAX_SEGMENTS frag_copy_rows
+ * copies in ONE launch, CTAs shared out in proportion to each segment's
+ * bytes.  The unshard of a whole FSDP parameter group out of one all-gather
+ * buffer: replaces the nine split_with_sizes -> clone chains of
+ *   v8/7815074de963/problem.py:18-75 and v8/94985bdb7630/problem.py:18-77
+ * (splits [512, 2097152, 524288, 524288, 2097152, 512, 7340032 x3] of the
+ * [8, 27264000] view), and the weight + table pair of
+ *   v5/013a3088b488/problem.py:18-36 and v8/8e33a91b7364/problem.py:18-51.
+ * Segments with rows == 0 or row_bytes == 0 are skipped; no destination may
+ * overlap a source or another destination.  When every segment is 16-byte
+ * aligned (pointers, strides, row_bytes) the group is one launch; otherwise
+ * each segment is copied by frag_copy_rows in turn.
+ * ------------------------------------------------------------------------- */
+#define FRAG_COPY_MAX_SEGMENTS 16
+
+typedef struct frag_copy_segment {
+  const void* src;
+  void* dst;
+  int64_t src_stride; /* bytes between source rows */
+  int64_t dst_stride; /* bytes between destination rows */
+  int64_t rows;
+  int64_t row_bytes;
+} frag_copy_segment;
+
+FRAG_API int frag_copy_rows_grouped(const frag_copy_segment* segs, int32_t n, frag_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Rotary position embedding on up to two tensors (q and k) in one launch.

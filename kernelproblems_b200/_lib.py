@@ -64,6 +64,20 @@ class RopeTensor(C.Structure):
     ]
 
 
+FRAG_COPY_MAX_SEGMENTS = 16
+
+
+class CopySegment(C.Structure):
+    _fields_ = [
+        ("src", _vp),
+        ("dst", _vp),
+        ("src_stride", _i64),
+        ("dst_stride", _i64),
+        ("rows", _i64),
+        ("row_bytes", _i64),
+    ]
+
+
 # name -> (restype, argtypes); mirrors include/frag.h one to one.
 SIGNATURES: dict[str, tuple] = {
     "frag_version": (C.c_char_p, []),
@@ -82,6 +96,9 @@ SIGNATURES: dict[str, tuple] = {
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     "frag_rmsnorm_bwd3": (
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp, _sz, _vp]),
+    "frag_rmsnorm_fwd_bwd": (
+        _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp,
+               _sz, _vp]),
     "frag_rmsnorm_bwd_num_blocks": (_i64, [_i64, _i64]),
     "frag_dw_reduce": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "frag_embedding_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
@@ -89,6 +106,7 @@ SIGNATURES: dict[str, tuple] = {
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
     "frag_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64]),
     "frag_copy_rows": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp]),
+    "frag_copy_rows_grouped": (_int, [C.POINTER(CopySegment), C.c_int32, _vp]),
     "frag_selftest_bounded_wait": (_int, [_i64, _vp]),
     "frag_rmsnorm_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "frag_rmsnorm_embedding_bwd": (

@@ -122,6 +122,13 @@ def bytes_rmsnorm_embedding_bwd(T: int, D: int, rows: int, n_dy: int = 3, dres: 
             + rows * D * F32 + D * F32)
 
 
+def bytes_rmsnorm_fwd_bwd(M: int, N: int, n_x: int, n_dy: int, dres: bool, y: bool) -> int:
+    # the forward recomputed in the backward: x terms, dy terms and dres read;
+    # y (when returned) and dx written; w read; dw written (fp32)
+    rows = n_x + n_dy + (1 if dres else 0) + (1 if y else 0) + 1
+    return rows * M * N * BF16 + N * BF16 + N * F32
+
+
 def bytes_add_rmsnorm_unshard(M: int, N: int, world: int, shard: int) -> int:
     # res, x read; y written (h and rstd are not outputs); the weight gathered
     # from `world` strided pieces (read + write); the table copied out of the

@@ -296,6 +296,12 @@ struct BwdIn {
   uint16_t* dx;
   float* partials;  // [G, N]
   float* rws;       // [M] rstd scratch (generic path)
+  // forward recomputed in the backward (FWD kernels only): the normalised
+  // input is h = bf16(bf16(x + x2) + x3), y = bf16((h * rstd) * w)
+  const uint16_t* x2;  // or nullptr
+  const uint16_t* x3;  // or nullptr (only with x2)
+  uint16_t* y;         // or nullptr
+  float* rstd_out;     // or nullptr
 };
 
 // One row block per CTA: rows [b*R, min(M, (b+1)*R)).  The next row's inputs
@@ -444,9 +450,15 @@ rmsnorm_bwd_vec(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block) {
 // row's inputs (dy, x, then dy2 and dres when present) into a ring of S
 // shared-memory stages, S rows ahead.  dweight partials stay in registers and
 // are written once per block, coalesced, like the register kernel above.
-template <int VPT, bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
+//
+// FWD: the forward recomputed in the same pass (activation checkpointing,
+// v6/822931829090/problem.py:19-66): x2 / x3 are streamed with the other
+// inputs and summed into h in bf16 before anything else reads the row; rstd
+// is recomputed from h and y (and rstd) are stored next to dx.
+template <int VPT, bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE, bool FWD = false>
 __global__ void __launch_bounds__(512)
 rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, int S, int* err) {
+  static_assert(!FWD || RECOMPUTE, "the fused forward recomputes rstd");
   // The dweight reduce that follows may be launched now; it waits for this
   // grid to finish before reading the partials.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -454,7 +466,12 @@ rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, in
   __shared__ float2 slots[2][32];
   __shared__ int s_abort;
   const bool has3 = HAS_DY2 && p.dy3 != nullptr;
-  const int nin = 2 + (HAS_DY2 ? 1 : 0) + (has3 ? 1 : 0) + (HAS_DRES ? 1 : 0);
+  const bool hasx2 = FWD && p.x2 != nullptr;
+  const bool hasx3 = hasx2 && p.x3 != nullptr;
+  // stage layout: dy, x, [dy2], [dy3], [dres], [x2], [x3]
+  const int sdres = 2 + (HAS_DY2 ? 1 : 0) + (has3 ? 1 : 0);
+  const int sx2 = sdres + (HAS_DRES ? 1 : 0);
+  const int nin = sx2 + (hasx2 ? 1 : 0) + (hasx3 ? 1 : 0);
   const int row_bytes = N * 2;
   const int stage_bytes = nin * row_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * stage_bytes);
@@ -482,6 +499,8 @@ rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, in
     if (HAS_DY2) bulk_g2s(st + (slot++) * row_bytes, p.dy2 + off, row_bytes, bar);
     if (has3) bulk_g2s(st + (slot++) * row_bytes, p.dy3 + off, row_bytes, bar);
     if (HAS_DRES) bulk_g2s(st + slot * row_bytes, p.dres + off, row_bytes, bar);
+    if (hasx2) bulk_g2s(st + sx2 * row_bytes, p.x2 + off, row_bytes, bar);
+    if (hasx3) bulk_g2s(st + (sx2 + 1) * row_bytes, p.x3 + off, row_bytes, bar);
     issued = i + 1;
   };
   if (threadIdx.x == 0)
@@ -510,6 +529,11 @@ rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, in
       if (c < chunks) {
         gdy[k] = *reinterpret_cast<const uint4*>(st + c * 16);
         gx[k] = *reinterpret_cast<const uint4*>(st + row_bytes + c * 16);
+        if (FWD && hasx2) {  // h = bf16(bf16(x + x2) + x3): bf16 tensors in the graph
+          gx[k] = add_bf16x8(gx[k], *reinterpret_cast<const uint4*>(st + sx2 * row_bytes + c * 16));
+          if (hasx3)
+            gx[k] = add_bf16x8(gx[k], *reinterpret_cast<const uint4*>(st + (sx2 + 1) * row_bytes + c * 16));
+        }
         if (HAS_DY2) {
           // Each partial sum of the gradients is a bf16 tensor in the graph.
           float g[8], g2[8];
@@ -526,8 +550,8 @@ rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, in
             gdy[k] = pack8(g);
           }
         }
-        if (HAS_DRES)  // dres is the last row of the stage
-          gdr[k] = *reinterpret_cast<const uint4*>(st + (nin - 1) * row_bytes + c * 16);
+        if (HAS_DRES)
+          gdr[k] = *reinterpret_cast<const uint4*>(st + sdres * row_bytes + c * 16);
       } else {
         gdy[k] = gx[k] = gdr[k] = make_uint4(0, 0, 0, 0);
       }
@@ -548,13 +572,16 @@ rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, in
     parity ^= 1;
     if (s_abort) break;
     if (threadIdx.x == 0) issue(i + S);  // stage i % S is free again
-    const float r = RECOMPUTE ? rsqrtf(tot.x * invN + eps) : rr;
+    // the fused forward rounds rstd like the forward kernel (sum / N)
+    const float r = FWD ? rsqrtf(tot.x / static_cast<float>(N) + eps)
+                        : (RECOMPUTE ? rsqrtf(tot.x * invN + eps) : rr);
+    if (FWD && p.rstd_out && threadIdx.x == 0) p.rstd_out[row] = r;
     const float cmean = r * tot.y * invN;  // mean(xhat * gw)
     const size_t base = static_cast<size_t>(row) * N;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int c = threadIdx.x + k * blockDim.x;
-      float g[8], xf[8], o[8];
+      float g[8], xf[8], o[8], yv[8];
       unpack8(gdy[k], g);
       unpack8(gx[k], xf);
       if (HAS_DRES) unpack8(gdr[k], o);
@@ -564,8 +591,10 @@ rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, in
         const float dx = (g[e] * wf[k][e] - xhat * cmean) * r;
         acc[k][e] = fmaf(g[e], xhat, acc[k][e]);
         o[e] = HAS_DRES ? o[e] + round_bf16(dx) : dx;
+        if (FWD) yv[e] = xhat * wf[k][e];
       }
       if (c < chunks) st_global(p.dx + base + c * 8, pack8(o));
+      if (FWD && p.y && c < chunks) st_global(p.y + base + c * 8, pack8(yv));
     }
   }
   if (threadIdx.x == 0 && s_abort)
@@ -588,9 +617,21 @@ rmsnorm_bwd_tma(BwdIn p, int64_t M, int N, float eps, int64_t rows_per_block, in
   }
 }
 
+// The normalised input of element i: x, or with the fused forward
+// h = bf16(bf16(x + x2) + x3).
+template <bool FWD>
+__device__ __forceinline__ float norm_input(const BwdIn& p, size_t i) {
+  float h = bf16_to_f(p.x[i]);
+  if (FWD && p.x2) {
+    h = round_bf16(h + bf16_to_f(p.x2[i]));
+    if (p.x3) h = round_bf16(h + bf16_to_f(p.x3[i]));
+  }
+  return h;
+}
+
 // Generic backward, pass 1: dx per row (one CTA per row), rstd copied or
-// recomputed into p.rws for pass 2.
-template <bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
+// recomputed into p.rws for pass 2 (with FWD also y and rstd_out).
+template <bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE, bool FWD = false>
 __global__ void __launch_bounds__(256)
 rmsnorm_bwd_generic_dx(BwdIn p, int64_t N, float eps) {
   __shared__ float2 slots[2][32];
@@ -601,28 +642,31 @@ rmsnorm_bwd_generic_dx(BwdIn p, int64_t N, float eps) {
     float g = bf16_to_f(p.dy[base + n]);
     if (HAS_DY2) g = round_bf16(g + bf16_to_f(p.dy2[base + n]));
     if (HAS_DY2 && p.dy3) g = round_bf16(g + bf16_to_f(p.dy3[base + n]));
-    const float xf = bf16_to_f(p.x[base + n]);
+    const float xf = norm_input<FWD>(p, base + n);
     if (RECOMPUTE) s1 = fmaf(xf, xf, s1);
     s2 = fmaf(xf, g * bf16_to_f(p.w[n]), s2);
   }
   const float2 tot = block_sum2(make_float2(s1, s2), slots, 0);
   const float invN = 1.0f / static_cast<float>(N);
-  const float r = RECOMPUTE ? rsqrtf(tot.x * invN + eps) : p.rstd[row];
+  const float r = FWD ? rsqrtf(tot.x / static_cast<float>(N) + eps)
+                      : (RECOMPUTE ? rsqrtf(tot.x * invN + eps) : p.rstd[row]);
   if (threadIdx.x == 0) p.rws[row] = r;
+  if (FWD && p.rstd_out && threadIdx.x == 0) p.rstd_out[row] = r;
   const float cmean = r * tot.y * invN;
   for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
     float g = bf16_to_f(p.dy[base + n]);
     if (HAS_DY2) g = round_bf16(g + bf16_to_f(p.dy2[base + n]));
     if (HAS_DY2 && p.dy3) g = round_bf16(g + bf16_to_f(p.dy3[base + n]));
-    const float xhat = bf16_to_f(p.x[base + n]) * r;
+    const float xhat = norm_input<FWD>(p, base + n) * r;
     const float dx = (g * bf16_to_f(p.w[n]) - xhat * cmean) * r;
     const float o = HAS_DRES ? bf16_to_f(p.dres[base + n]) + round_bf16(dx) : dx;
     p.dx[base + n] = f_to_bf16(o);
+    if (FWD && p.y) p.y[base + n] = f_to_bf16(xhat * bf16_to_f(p.w[n]));
   }
 }
 
 // Generic backward, pass 2: dweight partials, one thread per column per block.
-template <bool HAS_DY2>
+template <bool HAS_DY2, bool FWD = false>
 __global__ void __launch_bounds__(256)
 rmsnorm_bwd_generic_dw(BwdIn p, int64_t M, int64_t N, int64_t rows_per_block) {
   const int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -635,7 +679,7 @@ rmsnorm_bwd_generic_dw(BwdIn p, int64_t M, int64_t N, int64_t rows_per_block) {
     float g = bf16_to_f(p.dy[i]);
     if (HAS_DY2) g = round_bf16(g + bf16_to_f(p.dy2[i]));
     if (HAS_DY2 && p.dy3) g = round_bf16(g + bf16_to_f(p.dy3[i]));
-    acc = fmaf(g, bf16_to_f(p.x[i]) * p.rws[row], acc);
+    acc = fmaf(g, norm_input<FWD>(p, i) * p.rws[row], acc);
   }
   p.partials[static_cast<size_t>(blockIdx.y) * N + col] = acc;
 }
@@ -763,16 +807,17 @@ size_t bwd_workspace_bytes(const BwdPlan& pl, int64_t M, int64_t N) {
          align_up(static_cast<size_t>(M) * sizeof(float), 256);
 }
 
-template <bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE>
+template <bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE, bool FWD = false>
 int launch_bwd_t(const BwdPlan& pl, BwdIn p, int64_t M, int64_t N, float eps, cudaStream_t s) {
   const dim3 grid(static_cast<unsigned>(pl.G));
   const int T = pl.cfg.threads;
   if (pl.tma) {
-    const int nin = 2 + (HAS_DY2 ? 1 : 0) + (HAS_DY2 && p.dy3 ? 1 : 0) + (HAS_DRES ? 1 : 0);
+    const int nx = FWD && p.x2 ? (p.x3 ? 2 : 1) : 0;
+    const int nin = 2 + (HAS_DY2 ? 1 : 0) + (HAS_DY2 && p.dy3 ? 1 : 0) + (HAS_DRES ? 1 : 0) + nx;
     const int stage_bytes = nin * static_cast<int>(N) * 2;
     const int S = std::min(8, (220 * 1024 / pl.cps - 1024) / stage_bytes);
-    auto kern = pl.cfg.vpt == 1 ? rmsnorm_bwd_tma<1, HAS_DY2, HAS_DRES, RECOMPUTE>
-                                : rmsnorm_bwd_tma<2, HAS_DY2, HAS_DRES, RECOMPUTE>;
+    auto kern = pl.cfg.vpt == 1 ? rmsnorm_bwd_tma<1, HAS_DY2, HAS_DRES, RECOMPUTE, FWD>
+                                : rmsnorm_bwd_tma<2, HAS_DY2, HAS_DRES, RECOMPUTE, FWD>;
     const int smem = std::max(S, 1) * stage_bytes + 8 * std::max(S, 1);
     if (S >= 1 && allow_dynamic_smem(reinterpret_cast<const void*>(kern), smem)) {
       kern<<<grid, T, smem, s>>>(p, M, static_cast<int>(N), eps, pl.rows_per_block, S,
@@ -780,20 +825,18 @@ int launch_bwd_t(const BwdPlan& pl, BwdIn p, int64_t M, int64_t N, float eps, cu
       return check_launch();
     }
     // no room for the ring: the register-prefetch kernel on the same blocks
+    // (the fused forward takes the generic kernels)
   }
-  switch (pl.cfg.vpt) {
-    case 2:
-      rmsnorm_bwd_vec<2, HAS_DY2, HAS_DRES, RECOMPUTE><<<grid, T, 0, s>>>(p, M, static_cast<int>(N), eps, pl.rows_per_block);
-      break;
-    default: {
-      rmsnorm_bwd_generic_dx<HAS_DY2, HAS_DRES, RECOMPUTE>
-          <<<dim3(static_cast<unsigned>(M)), 256, 0, s>>>(p, N, eps);
-      int st = check_launch();
-      if (st != FRAG_OK) return st;
-      const dim3 g2(static_cast<unsigned>(ceil_div(N, 256)), static_cast<unsigned>(pl.G));
-      rmsnorm_bwd_generic_dw<HAS_DY2><<<g2, 256, 0, s>>>(p, M, N, pl.rows_per_block);
-    }
+  if (!FWD && pl.cfg.vpt == 2) {
+    rmsnorm_bwd_vec<2, HAS_DY2, HAS_DRES, RECOMPUTE><<<grid, T, 0, s>>>(p, M, static_cast<int>(N), eps, pl.rows_per_block);
+    return check_launch();
   }
+  rmsnorm_bwd_generic_dx<HAS_DY2, HAS_DRES, RECOMPUTE, FWD>
+      <<<dim3(static_cast<unsigned>(M)), 256, 0, s>>>(p, N, eps);
+  int st = check_launch();
+  if (st != FRAG_OK) return st;
+  const dim3 g2(static_cast<unsigned>(ceil_div(N, 256)), static_cast<unsigned>(pl.G));
+  rmsnorm_bwd_generic_dw<HAS_DY2, FWD><<<g2, 256, 0, s>>>(p, M, N, pl.rows_per_block);
   return check_launch();
 }
 
@@ -801,6 +844,79 @@ int launch_bwd_t(const BwdPlan& pl, BwdIn p, int64_t M, int64_t N, float eps, cu
 }  // namespace frag
 
 using namespace frag;
+
+namespace {
+
+// frag_rmsnorm_bwd3 (fwd == false) and frag_rmsnorm_fwd_bwd (fwd == true:
+// rstd recomputed from h = x [+ x2 [+ x3]], y / rstd stored when given).
+int rmsnorm_bwd_impl(bool fwd, const void* dy, const void* dy2, const void* dy3, const void* x,
+                     const void* x2, const void* x3, const float* rstd, const void* w,
+                     const void* dres, void* y_out, float* rstd_out, void* dx_out, float* dw,
+                     void* dw_bf16, int64_t M, int64_t N, float eps, void* workspace,
+                     size_t workspace_bytes, frag_stream_t stream) {
+  if (M < 0 || N < 0) return FRAG_ERR_INVALID_ARG;
+  if (dy3 && !dy2) return FRAG_ERR_INVALID_ARG;
+  if (N == 0 && M > 0) return FRAG_ERR_SHAPE;
+  if (M > 0 && (!dy || !x || !w || !dx_out)) return FRAG_ERR_INVALID_ARG;
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL) return FRAG_ERR_SHAPE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (M == 0) {
+    // Empty batch: dweight is an empty sum.
+    if (dw && cuda_status(cudaMemsetAsync(dw, 0, N * sizeof(float), s)) != FRAG_OK)
+      return FRAG_ERR_CUDA;
+    if (dw_bf16 && cuda_status(cudaMemsetAsync(dw_bf16, 0, N * 2, s)) != FRAG_OK)
+      return FRAG_ERR_CUDA;
+    return FRAG_OK;
+  }
+  bool aligned = aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx_out);
+  if (dy2) aligned = aligned && aligned16(dy2);
+  if (dy3) aligned = aligned && aligned16(dy3);
+  if (dres) aligned = aligned && aligned16(dres);
+  if (x2) aligned = aligned && aligned16(x2);
+  if (x3) aligned = aligned && aligned16(x3);
+  if (y_out) aligned = aligned && aligned16(y_out);
+  const BwdPlan pl = make_bwd_plan(M, N, aligned);
+  if (!workspace || workspace_bytes < bwd_workspace_bytes(pl, M, N)) return FRAG_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return FRAG_ERR_ALIGN;
+
+  BwdIn p;
+  p.dy = static_cast<const uint16_t*>(dy);
+  p.dy2 = static_cast<const uint16_t*>(dy2);
+  p.dy3 = static_cast<const uint16_t*>(dy3);
+  p.x = static_cast<const uint16_t*>(x);
+  p.rstd = rstd;
+  p.w = static_cast<const uint16_t*>(w);
+  p.dres = static_cast<const uint16_t*>(dres);
+  p.dx = static_cast<uint16_t*>(dx_out);
+  p.partials = static_cast<float*>(workspace);
+  p.rws = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                   align_up(static_cast<size_t>(pl.G) * N * sizeof(float), 256));
+  p.x2 = static_cast<const uint16_t*>(x2);
+  p.x3 = static_cast<const uint16_t*>(x3);
+  p.y = static_cast<uint16_t*>(y_out);
+  p.rstd_out = rstd_out;
+
+  const bool rc = (rstd == nullptr);
+  int st;
+  if (fwd) {
+    if (dy2) st = dres ? launch_bwd_t<true, true, true, true>(pl, p, M, N, eps, s)
+                       : launch_bwd_t<true, false, true, true>(pl, p, M, N, eps, s);
+    else st = dres ? launch_bwd_t<false, true, true, true>(pl, p, M, N, eps, s)
+                   : launch_bwd_t<false, false, true, true>(pl, p, M, N, eps, s);
+  } else if (dy2) {
+    if (dres) st = rc ? launch_bwd_t<true, true, true>(pl, p, M, N, eps, s) : launch_bwd_t<true, true, false>(pl, p, M, N, eps, s);
+    else st = rc ? launch_bwd_t<true, false, true>(pl, p, M, N, eps, s) : launch_bwd_t<true, false, false>(pl, p, M, N, eps, s);
+  } else {
+    if (dres) st = rc ? launch_bwd_t<false, true, true>(pl, p, M, N, eps, s) : launch_bwd_t<false, true, false>(pl, p, M, N, eps, s);
+    else st = rc ? launch_bwd_t<false, false, true>(pl, p, M, N, eps, s) : launch_bwd_t<false, false, false>(pl, p, M, N, eps, s);
+  }
+  if (st != FRAG_OK) return st;
+  if (dw || dw_bf16)
+    return launch_dw_reduce(p.partials, pl.G, N, dw, static_cast<uint16_t*>(dw_bf16), s, pl.tma);
+  return FRAG_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -851,54 +967,18 @@ int frag_rmsnorm_bwd3(const void* dy, const void* dy2, const void* dy3, const vo
                       const float* rstd, const void* w, const void* dres, void* dx_out, float* dw,
                       void* dw_bf16, int64_t M, int64_t N, float eps, void* workspace,
                       size_t workspace_bytes, frag_stream_t stream) {
-  if (M < 0 || N < 0) return FRAG_ERR_INVALID_ARG;
-  if (dy3 && !dy2) return FRAG_ERR_INVALID_ARG;
-  if (N == 0 && M > 0) return FRAG_ERR_SHAPE;
-  if (M > 0 && (!dy || !x || !w || !dx_out)) return FRAG_ERR_INVALID_ARG;
-  if (M > 0x7fffffffLL || N > 0x7fffffffLL) return FRAG_ERR_SHAPE;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (M == 0) {
-    // Empty batch: dweight is an empty sum.
-    if (dw && cuda_status(cudaMemsetAsync(dw, 0, N * sizeof(float), s)) != FRAG_OK)
-      return FRAG_ERR_CUDA;
-    if (dw_bf16 && cuda_status(cudaMemsetAsync(dw_bf16, 0, N * 2, s)) != FRAG_OK)
-      return FRAG_ERR_CUDA;
-    return FRAG_OK;
-  }
-  bool aligned = aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx_out);
-  if (dy2) aligned = aligned && aligned16(dy2);
-  if (dy3) aligned = aligned && aligned16(dy3);
-  if (dres) aligned = aligned && aligned16(dres);
-  const BwdPlan pl = make_bwd_plan(M, N, aligned);
-  if (!workspace || workspace_bytes < bwd_workspace_bytes(pl, M, N)) return FRAG_ERR_WORKSPACE;
-  if (!aligned16(workspace)) return FRAG_ERR_ALIGN;
+  return rmsnorm_bwd_impl(false, dy, dy2, dy3, x, nullptr, nullptr, rstd, w, dres, nullptr, nullptr,
+                          dx_out, dw, dw_bf16, M, N, eps, workspace, workspace_bytes, stream);
+}
 
-  BwdIn p;
-  p.dy = static_cast<const uint16_t*>(dy);
-  p.dy2 = static_cast<const uint16_t*>(dy2);
-  p.dy3 = static_cast<const uint16_t*>(dy3);
-  p.x = static_cast<const uint16_t*>(x);
-  p.rstd = rstd;
-  p.w = static_cast<const uint16_t*>(w);
-  p.dres = static_cast<const uint16_t*>(dres);
-  p.dx = static_cast<uint16_t*>(dx_out);
-  p.partials = static_cast<float*>(workspace);
-  p.rws = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                   align_up(static_cast<size_t>(pl.G) * N * sizeof(float), 256));
-
-  const bool rc = (rstd == nullptr);
-  int st;
-  if (dy2) {
-    if (dres) st = rc ? launch_bwd_t<true, true, true>(pl, p, M, N, eps, s) : launch_bwd_t<true, true, false>(pl, p, M, N, eps, s);
-    else st = rc ? launch_bwd_t<true, false, true>(pl, p, M, N, eps, s) : launch_bwd_t<true, false, false>(pl, p, M, N, eps, s);
-  } else {
-    if (dres) st = rc ? launch_bwd_t<false, true, true>(pl, p, M, N, eps, s) : launch_bwd_t<false, true, false>(pl, p, M, N, eps, s);
-    else st = rc ? launch_bwd_t<false, false, true>(pl, p, M, N, eps, s) : launch_bwd_t<false, false, false>(pl, p, M, N, eps, s);
-  }
-  if (st != FRAG_OK) return st;
-  if (dw || dw_bf16)
-    return launch_dw_reduce(p.partials, pl.G, N, dw, static_cast<uint16_t*>(dw_bf16), s, pl.tma);
-  return FRAG_OK;
+int frag_rmsnorm_fwd_bwd(const void* x, const void* x2, const void* x3, const void* w,
+                         const void* dy, const void* dy2, const void* dy3, const void* dres,
+                         void* y_out, float* rstd_out, void* dx_out, float* dw, void* dw_bf16,
+                         int64_t M, int64_t N, float eps, void* workspace, size_t workspace_bytes,
+                         frag_stream_t stream) {
+  if (x3 && !x2) return FRAG_ERR_INVALID_ARG;
+  return rmsnorm_bwd_impl(true, dy, dy2, dy3, x, x2, x3, nullptr, w, dres, y_out, rstd_out, dx_out,
+                          dw, dw_bf16, M, N, eps, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

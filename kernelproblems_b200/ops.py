@@ -26,6 +26,7 @@ __all__ = [
     "rmsnorm_fwd",
     "add_rmsnorm_fwd",
     "rmsnorm_bwd",
+    "rmsnorm_fwd_bwd",
     "rmsnorm_bwd_workspace_bytes",
     "rmsnorm_bwd_num_blocks",
     "dw_reduce",
@@ -34,6 +35,7 @@ __all__ = [
     "embedding_bwd",
     "rmsnorm_embedding_bwd",
     "copy_rows",
+    "copy_rows_grouped",
     "rope",
     "check_status",
     "reset_status",
@@ -167,6 +169,56 @@ def add_rmsnorm_fwd(residual: torch.Tensor, x: torch.Tensor, weight: torch.Tenso
         _lib.call("frag_add_rmsnorm_fwd", _ptr(residual), _ptr(x), _ptr(wc),
                   _ptr(h), _ptr(y), _ptr(rstd), M, N, float(eps), _stream(x.device))
     return h, y, rstd
+
+
+def rmsnorm_fwd_bwd(x: torch.Tensor, weight: torch.Tensor, dy: torch.Tensor, *,
+                    x2: torch.Tensor | None = None, x3: torch.Tensor | None = None,
+                    dy2: torch.Tensor | None = None, dy3: torch.Tensor | None = None,
+                    dres: torch.Tensor | None = None, eps: float = 1e-5,
+                    write_y: bool = True, save_rstd: bool = False,
+                    dw_dtype: torch.dtype | None = torch.float32,
+                    workspace: torch.Tensor | None = None):
+    """RMSNorm forward recomputed inside its backward, one pass
+    (frag_rmsnorm_fwd_bwd).  Returns (y, rstd, dx, dw):
+
+    h     bf16(bf16(x + x2) + x3) (x2, x3 optional), never written
+    y     bf16((h * rstd) * w) like x, or None (write_y=False)
+    rstd  fp32 [rows], or None (save_rstd=False)
+    dx    bf16(dres + bf16(RMSNorm backward of bf16(bf16(dy + dy2) + dy3)))
+    dw    fp32, bf16 or None, summed in a fixed order
+    """
+    _need(x, "x", torch.bfloat16)
+    dev = x.device
+    _need(weight, "weight", torch.bfloat16, dev)
+    N = weight.numel()
+    M = _rows(x, N, "x")
+    if x3 is not None and x2 is None:
+        raise ValueError("x3 needs x2 (the inputs are summed in order)")
+    if dy3 is not None and dy2 is None:
+        raise ValueError("dy3 needs dy2 (the gradients are summed in order)")
+    for name, t in (("dy", dy), ("x2", x2), ("x3", x3), ("dy2", dy2), ("dy3", dy3), ("dres", dres)):
+        if t is not None:
+            _need(t, name, torch.bfloat16, dev)
+            if t.shape != x.shape:
+                raise ValueError(f"{name} {tuple(t.shape)} and x {tuple(x.shape)} differ")
+            _rows(t, N, name)
+    if dw_dtype not in (None, torch.float32, torch.bfloat16):
+        raise TypeError("dw_dtype must be float32, bfloat16 or None")
+    y = torch.empty_like(x) if write_y else None
+    rstd = torch.empty(M, dtype=torch.float32, device=dev) if save_rstd else None
+    dx = torch.empty_like(x)
+    dw = None if dw_dtype is None else torch.empty(N, dtype=dw_dtype, device=dev)
+    with _on_device(dev):
+        lib = _lib.load()
+        need = int(lib.frag_rmsnorm_bwd_workspace_bytes(M, N))
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+        _lib.call("frag_rmsnorm_fwd_bwd", _ptr(x), _ptr(x2), _ptr(x3), _ptr(weight.contiguous()),
+                  _ptr(dy), _ptr(dy2), _ptr(dy3), _ptr(dres), _ptr(y), _ptr(rstd), _ptr(dx),
+                  _ptr(dw) if dw_dtype == torch.float32 else None,
+                  _ptr(dw) if dw_dtype == torch.bfloat16 else None,
+                  M, N, float(eps), _ptr(workspace), workspace.numel(), _stream(dev))
+    return y, rstd, dx, dw
 
 
 def rmsnorm_bwd_workspace_bytes(M: int, N: int, device=None) -> int:
@@ -424,12 +476,7 @@ def copy_rows(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     """Contiguous copy of a 2-D tensor whose rows are contiguous but may be
     strided apart (a split of an FSDP all-gather buffer viewed [world, -1]).
     Returns a new [rows, cols] tensor (or fills `out`)."""
-    if not isinstance(src, torch.Tensor):
-        raise TypeError("src must be a torch.Tensor")
-    if not src.is_cuda:
-        raise ValueError("src must be a CUDA tensor")
-    if src.dim() != 2 or (src.shape[1] > 1 and src.stride(1) != 1):
-        raise ValueError("src must be 2-D with contiguous rows")
+    _check_copy_src(src)
     rows, cols = src.shape
     if out is None:
         out = torch.empty(rows, cols, dtype=src.dtype, device=src.device)
@@ -440,6 +487,50 @@ def copy_rows(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
         _lib.call("frag_copy_rows", _ptr(src), src.stride(0) * es, _ptr(out), cols * es, rows,
                   cols * es, _stream(src.device))
     return out
+
+
+def _check_copy_src(src: torch.Tensor) -> None:
+    if not isinstance(src, torch.Tensor):
+        raise TypeError("src must be a torch.Tensor")
+    if not src.is_cuda:
+        raise ValueError("src must be a CUDA tensor")
+    if src.dim() != 2 or (src.shape[1] > 1 and src.stride(1) != 1):
+        raise ValueError("src must be 2-D with contiguous rows")
+
+
+def copy_rows_grouped(srcs, outs=None) -> list[torch.Tensor]:
+    """copy_rows for up to 16 sources in one launch (frag_copy_rows_grouped):
+    the splits of one FSDP all-gather buffer viewed [world, -1].  Returns the
+    contiguous copies in order (or fills the given `outs`, None entries
+    allocated)."""
+    srcs = list(srcs)
+    if len(srcs) > _lib.FRAG_COPY_MAX_SEGMENTS:
+        raise ValueError(f"at most {_lib.FRAG_COPY_MAX_SEGMENTS} sources per group")
+    outs = [None] * len(srcs) if outs is None else list(outs)
+    if len(outs) != len(srcs):
+        raise ValueError("outs must match srcs in length")
+    if not srcs:
+        return []
+    for src in srcs:
+        _check_copy_src(src)
+    dev = srcs[0].device
+    if any(src.device != dev for src in srcs):
+        raise ValueError("all sources must be on one device")
+    segs = (_lib.CopySegment * len(srcs))()
+    for i, src in enumerate(srcs):
+        rows, cols = src.shape
+        out = outs[i]
+        if out is None:
+            out = outs[i] = torch.empty(rows, cols, dtype=src.dtype, device=dev)
+        elif (out.shape != src.shape or out.dtype != src.dtype or not out.is_contiguous()
+              or out.device != dev):
+            raise ValueError("each out must be a contiguous tensor of its src's shape and dtype")
+        es = src.element_size()
+        segs[i] = _lib.CopySegment(src.data_ptr(), out.data_ptr(), src.stride(0) * es, cols * es,
+                                   rows, cols * es)
+    with _on_device(dev):
+        _lib.call("frag_copy_rows_grouped", segs, len(srcs), _stream(dev))
+    return outs
 
 
 # ------------------------------------------------------------------- RoPE

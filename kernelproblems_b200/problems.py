@@ -58,8 +58,32 @@ def rms_fwd_59f786beb25f(embedding, weight):
 
 
 def _fsdp_weight(shard_view: torch.Tensor) -> torch.Tensor:
-    # [8, 512] strided view of the all-gathered flat buffer -> contiguous [4096]
-    return shard_view.contiguous().view(-1)
+    # [8, 512] view of the all-gathered flat buffer -> contiguous [4096] (a
+    # copy only when the shards are strided apart)
+    if shard_view.is_contiguous():
+        return shard_view.view(-1)
+    return ops.copy_rows(shard_view).view(-1)
+
+
+WORLD = 8   # FSDP ranks whose shards one all-gather buffer holds
+
+
+def _splits(flat: torch.Tensor, sizes) -> tuple:
+    """split_with_sizes(flat.view(8, -1), sizes, 1): strided views, no copy."""
+    return torch.split(flat.view(WORLD, -1), list(sizes), dim=1)
+
+
+def _add_rms_weight0(mm, res, w):
+    _, y, _ = ops.add_rmsnorm_fwd(res.contiguous(), mm.contiguous().view(res.shape), w.view(-1), 1e-5,
+                                  write_h=False, save_rstd=False)
+    return y.view(-1, w.numel())
+
+
+def _add_rms_table(mm, res, flat):
+    # splits [512, 65667072]: the norm weight and the unsharded lm_head /
+    # embedding table, both copied out in one grouped launch
+    w, table = ops.copy_rows_grouped(_splits(flat, [512, flat.numel() // WORLD - 512]))
+    return _add_rms_weight0(mm, res, w), table.view(VOCAB, DIM)
 
 
 def add_rms_unshard_8e33a91b7364(mm_223, add_62, wait_tensor_969):
@@ -68,17 +92,58 @@ def add_rms_unshard_8e33a91b7364(mm_223, add_62, wait_tensor_969):
     [8, 512] split 0 of the all-gather buffer viewed [8, -1], and the
     [8, 65667072] split 1 unsharded into a contiguous [128256, 4096] table ->
     (y [M, N], table)."""
-    flat = wait_tensor_969.view(8, -1)
-    w = ops.copy_rows(flat[:, :512]).view(-1)
-    _, y, _ = ops.add_rmsnorm_fwd(add_62.contiguous(), mm_223.contiguous().view(add_62.shape), w,
-                                  1e-5, write_h=False, save_rstd=False)
-    table = ops.copy_rows(flat[:, 512:]).view(VOCAB, DIM)
-    return (y.view(-1, w.numel()), table)
+    return _add_rms_table(mm_223, add_62, wait_tensor_969)
+
+
+def add_rms_unshard_t_013a3088b488(mm_223, add_62, wait_tensor_969):
+    """v5/013a3088b488/problem.py:15-40: as v8/8e33a91b7364, with the table
+    returned transposed for the lm_head -> (y [M, N], table.t() [4096, 128256])."""
+    y, table = _add_rms_table(mm_223, add_62, wait_tensor_969)
+    return (y, table.t())
+
+
+def add_rms_unshard_tt_18b859c50de2(mm_223, add_62, wait_tensor_969):
+    """v4/18b859c50de2/problem.py:12-33 (v1-v3 same id): v5/013a3088b488's
+    graph with reshape for _unsafe_view and the table transposed twice, so
+    the second output is the contiguous [128256, 4096] table itself."""
+    y, table = _add_rms_table(mm_223, add_62, wait_tensor_969)
+    return (y, table.t().t())
+
+
+# splits of one decoder layer's parameters in the [8, 27264000] view of its
+# all-gather buffer, and the shapes they are unsharded into (the ninth split
+# is not used by the graph)
+LAYER_SPLITS = (512, 2097152, 524288, 524288, 2097152, 512, 7340032, 7340032, 7340032)
+LAYER_SHAPES = ((4096,), (4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (4096,),
+                (14336, 4096), (14336, 4096))
+
+
+def _add_rms_layer(mm, res, flat):
+    parts = ops.copy_rows_grouped(_splits(flat, LAYER_SPLITS)[:len(LAYER_SHAPES)])
+    y = _add_rms_weight0(mm, res, parts[0])
+    return y, [c.view(shape) for c, shape in zip(parts, LAYER_SHAPES)], parts
+
+
+def add_rms_layer_unshard_94985bdb7630(mm_216, add_60, wait_tensor_966):
+    """v8/94985bdb7630/problem.py:14-79: h = add_60 + mm_216, y =
+    _fused_rms_norm(h, split 0 as the weight, 1e-5), and splits 1-7 of the
+    [8, 27264000] view unsharded -> (y x3 [8192, 4096], [4096, 4096],
+    [1024, 4096], [1024, 4096], [4096, 4096], [4096], [14336, 4096] x2)."""
+    y, shaped, _ = _add_rms_layer(mm_216, add_60, wait_tensor_966)
+    return (y, y, y, *shaped[1:])
+
+
+def add_rms_layer_unshard_7815074de963(mm_209, add_58, wait_tensor_963):
+    """v8/7815074de963/problem.py:14-77: as v8/94985bdb7630, with split 7
+    returned as the raw contiguous clone [8, 7340032]."""
+    y, shaped, parts = _add_rms_layer(mm_209, add_58, wait_tensor_963)
+    return (y, y, y, *shaped[1:7], parts[7])
 
 
 def rms_fwd_215dd2e6a519(getitem_1614, add_61):
-    """v7/215dd2e6a519/problem.py:10-24: weight gathered from the FSDP shard
-    view, _fused_rms_norm -> three [M,N] views of y."""
+    """v7/215dd2e6a519/problem.py:10-24 (v1-v4/84496d824942 the same graph
+    with reshape): weight gathered from the FSDP shard view, _fused_rms_norm
+    -> three [M,N] views of y."""
     w = _fsdp_weight(getitem_1614)
     y, _ = ops.rmsnorm_fwd(add_61.contiguous(), w, 1e-5, save_rstd=False)
     y2 = y.view(-1, w.numel())
@@ -91,6 +156,18 @@ def rms_fwd_ac3fb0b7281f(getitem_1619, add_62):
     y, _ = ops.rmsnorm_fwd(add_62.contiguous(), w, 1e-5, save_rstd=False)
     y2 = y.view(-1, w.numel())
     return (y2, y2)
+
+
+def rms_fwd_ffn_unshard_2a844503364a(getitem_1619, add_62, getitem_1620, getitem_1621, getitem_1622):
+    """v4/2a844503364a/problem.py:18-74 (v1-v3 same id): ac3fb0b7281f's
+    norm, plus the three FFN weights unsharded from their [8, 7340032] views
+    of the all-gather buffers and returned transposed -> (y x2, w1.t()
+    [4096, 14336], w3.t() [4096, 14336], w2.t() [14336, 4096]).  The weight
+    and the three matrices are copied in one grouped launch."""
+    w, a, b, c = ops.copy_rows_grouped([getitem_1619, getitem_1620, getitem_1621, getitem_1622])
+    y, _ = ops.rmsnorm_fwd(add_62.contiguous(), w.view(-1), 1e-5, save_rstd=False)
+    y2 = y.view(-1, w.numel())
+    return (y2, y2, a.view(14336, 4096).t(), b.view(14336, 4096).t(), c.view(4096, 14336).t())
 
 
 def add_rms_fwd_7884328a5557(mm_220, add_61, w):
@@ -171,6 +248,93 @@ def add3_rms_bwd_ed20955ec34b(mm_672, view_1794, mm_674, embedding, getitem_1_re
                                dy3=mm_674.contiguous().view(x.shape),
                                dres=add_220.contiguous(), dw_dtype=torch.float32)
     return dres, dw
+
+
+# ------------------------------- RMSNorm forward recomputed in its backward
+
+
+def _recompute_bwd(w, x, dys, *, xs=(), dres=None, write_y=True):
+    """One frag_rmsnorm_fwd_bwd pass: h = x [+ xs...] (bf16 adds in order),
+    y = RMSNorm(h) when asked, dh of the summed gradients, dres added,
+    dweight fp32 -> (y [M, N] or None, dx like x, dweight)."""
+    x = x.contiguous()
+    v = [t.contiguous().view(x.shape) for t in dys]
+    vx = [t.contiguous().view(x.shape) for t in xs]
+    y, _, dx, dw = ops.rmsnorm_fwd_bwd(
+        x, w, v[0], x2=vx[0] if vx else None, x3=vx[1] if len(vx) > 1 else None,
+        dy2=v[1] if len(v) > 1 else None, dy3=v[2] if len(v) > 2 else None,
+        dres=None if dres is None else dres.contiguous(), eps=1e-5, write_y=write_y,
+        dw_dtype=torch.float32)
+    return (None if y is None else y.view(-1, w.numel())), dx, dw
+
+
+def rms_fwd_bwd3_822931829090(add_1, _unsafe_view_450, mm_656, mm_658, mm_660, add_215):
+    """v6/822931829090/problem.py:19-66: y, rstd = _fused_rms_norm(add_1),
+    dy = (mm_656 + mm_658) + mm_660, dx = add_215 + _fused_rms_norm_backward
+    -> (y x3 [M, N], dx, dweight fp32), one pass."""
+    y, dx, dw = _recompute_bwd(_unsafe_view_450, add_1, (mm_656, mm_658, mm_660), dres=add_215)
+    return (y, y, y, dx, dw)
+
+
+def rms_fwd_bwd3_363b7b58c971(getitem_818, add_1, mm_656, mm_658, mm_660, add_215):
+    """v4/363b7b58c971/problem.py:19-75 (v1-v3 same id, v5/92ce4a0c7b2c):
+    822931829090 with the weight gathered from its [8, 512] FSDP view."""
+    return rms_fwd_bwd3_822931829090(add_1, _fsdp_weight(getitem_818), mm_656, mm_658, mm_660,
+                                     add_215)
+
+
+def rms_fwd_bwd2_e9198b707240(add_62_recomputed, _unsafe_view_986, mm_230, mm_232, getitem_420):
+    """v6/e9198b707240/problem.py:18-56: y, rstd = _fused_rms_norm(x),
+    dy = mm_230 + mm_232, dx = getitem_420 + backward -> (y x2, dx, dweight)."""
+    y, dx, dw = _recompute_bwd(_unsafe_view_986, add_62_recomputed, (mm_230, mm_232),
+                               dres=getitem_420)
+    return (y, y, dx, dw)
+
+
+def rms_fwd_bwd2_84c0a03c4374(getitem_1624, add_62_recomputed, mm_230, mm_232, getitem_420):
+    """v4/84c0a03c4374/problem.py:18-65 (v1-v3 same id, v5/401b52261ef5):
+    e9198b707240 with the weight from its [8, 512] FSDP view."""
+    return rms_fwd_bwd2_e9198b707240(add_62_recomputed, _fsdp_weight(getitem_1624), mm_230, mm_232,
+                                     getitem_420)
+
+
+def add_rms_fwd_bwd_408ac0979ac5(mm_3, embedding, _unsafe_view_428, mm_664, mm_666, add_218):
+    """v6/408ac0979ac5/problem.py:19-63: h = embedding + mm_3 (bf16, never
+    written), y, rstd = _fused_rms_norm(h), dy = mm_664 + mm_666, dx =
+    add_218 + backward at h -> (y x2, dx, dweight)."""
+    y, dx, dw = _recompute_bwd(_unsafe_view_428, embedding, (mm_664, mm_666), xs=(mm_3,),
+                               dres=add_218)
+    return (y, y, dx, dw)
+
+
+def add_rms_fwd_bwd_9c745ea697a7(mm_3, embedding, getitem_787, mm_664, mm_666, add_218):
+    """v4/9c745ea697a7/problem.py:19-72 (v1-v3 same id, v5/cbfdd7549926):
+    408ac0979ac5 with the weight from its [8, 512] FSDP view."""
+    return add_rms_fwd_bwd_408ac0979ac5(mm_3, embedding, _fsdp_weight(getitem_787), mm_664, mm_666,
+                                        add_218)
+
+
+def add_rms_bwd_28b45679fca1(mm_223, add_62_recomputed, mm_226, view_3253):
+    """v6/28b45679fca1/problem.py:17-41: h = add_62_recomputed + mm_223, rstd
+    of h recomputed, dh = _fused_rms_norm_backward(mm_226, h) -> (dh,
+    dweight fp32); h and y are never written."""
+    _, dx, dw = _recompute_bwd(view_3253, add_62_recomputed, (mm_226,), xs=(mm_223,), write_y=False)
+    return (dx, dw)
+
+
+def add_rms_bwd_f7ad66842c19(mm_223, add_62_recomputed, mm_226, wait_tensor_970):
+    """v4/f7ad66842c19/problem.py:17-48 (v1-v3 same id, v5/ac7d64b3c769):
+    28b45679fca1 with the weight the [4096] buffer viewed [8, 512], split
+    [512] and viewed back (no copy in the graph either)."""
+    return add_rms_bwd_28b45679fca1(mm_223, add_62_recomputed, mm_226,
+                                    _fsdp_weight(wait_tensor_970.view(WORLD, -1)))
+
+
+def add2_rms_bwd_3c6c589cdf81(mm_220, add_61, mm_223, mm_226, view_3253):
+    """v8/3c6c589cdf81/problem.py:18-53: h = (add_61 + mm_220) + mm_223
+    (bf16), rstd recomputed, dh = backward(mm_226, h) -> (dh [M, N], dweight)."""
+    _, dx, dw = _recompute_bwd(view_3253, add_61, (mm_226,), xs=(mm_220, mm_223), write_y=False)
+    return (dx.view(-1, view_3253.numel()), dw)
 
 
 # ---------------------------------------------------------------- embedding
@@ -276,29 +440,44 @@ def rope_bwd_03d64c25b654(_conj_62, getitem_642):
     return _rope_bwd_strided(getitem_642, _conj_62)
 
 
-# ------------------------------------------------- SURVEY "next" fusions
+def rope_bwd_dc55b25cdcb2(_conj_63, getitem_641):
+    """v6/dc55b25cdcb2/problem.py:15-43: clone(conj freqs) x q-grad
+    [1, 32, S, 128] (a transposed view) -> [S, 4096]."""
+    return _rope_bwd_strided(getitem_641, _conj_63)
 
-_SPLITS_873 = [512, 2097152, 524288, 524288, 2097152, 512, 7340032, 7340032, 7340032]
-_SHAPES_873 = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (4096,), (14336, 4096)]
 
+def rope_bwd_qkv_a1318bc813d2(_conj_62, _conj_63, getitem_641, getitem_642, getitem_643):
+    """v4/a1318bc813d2/problem.py:18-85 (v5/a1bb72d946b0 with view for
+    reshape): q-grad x _conj_63 and k-grad x _conj_62 (two tables, two
+    launches), each viewed [S, H*128] and transposed; the v-grad passes
+    through as the same transposed view of its storage (no copy, as in the
+    graph) -> (dq.t() [4096, S], dk.t() [1024, S], dv.t() [1024, S])."""
+    dq = _rope_bwd_strided(getitem_641, _conj_63)
+    dk = _rope_bwd_strided(getitem_642, _conj_62)
+    _, H, S, D = getitem_643.shape
+    dv = getitem_643.transpose(1, 2).reshape(1, S, H * D).reshape(S, H * D)
+    return (dq.t(), dk.t(), dv.t())
+
+
+# ------------------------------------------ fused chains across the path
 
 def emb_rms_12545c1e9b06(wait_tensor_871, arg583_1, wait_tensor_873):
     """v8/12545c1e9b06/optimized_kernel.py:66: embedding gather fused with the
     first attention_norm RMSNorm (eps 1e-5), the norm weight taken from split 0
     of the second FSDP buffer (problem.py:27-39); the gathered rows are never
     written to HBM.  Also returns the contiguous copies of splits 1-6 the graph
-    makes (FSDP unshard copies: plain data movement, done with torch)."""
+    makes, unsharded with the weight in one grouped copy."""
     table = wait_tensor_871.view(VOCAB, DIM)
-    parts = wait_tensor_873.view(8, -1).split(_SPLITS_873, dim=1)
-    w = parts[0].contiguous().view(-1)
-    y, _, _ = ops.embedding_rmsnorm_fwd(arg583_1, table, w, 1e-5)
+    parts = ops.copy_rows_grouped(_splits(wait_tensor_873, LAYER_SPLITS)[:7])
+    y, _, _ = ops.embedding_rmsnorm_fwd(arg583_1, table, parts[0].view(-1), 1e-5)
     y2 = y.view(-1, DIM)
-    clones = [parts[i + 1].contiguous().view(_SHAPES_873[i]) for i in range(6)]
+    clones = [c.view(shape) for c, shape in zip(parts[1:7], LAYER_SHAPES[1:7])]
     return (y2, y2, y2, *clones)
 
 
 def rope_sdpa_6b92d6e665ab(arg586_1, arg582_1, mm_217, mm_218):
-    """v4/6b92d6e665ab/optimized_kernel.py: q and k RoPE returned as the
+    """v4/6b92d6e665ab/optimized_kernel.py (v5/ca76bd89ec38 the same graph
+    with _unsafe_view): q and k RoPE returned as the
     [1, H, S, 128] transposed views attention consumes; the reference graph
     computes each twice, so two independent results are returned too."""
     S = mm_217.shape[0]
@@ -355,9 +534,13 @@ PROBLEMS: dict[str, Callable] = {
     "v6/0b493aad68f0": norm_emb_bwd_0b493aad68f0,
     "v5/118d525f44e0": norm_emb_bwd_118d525f44e0,
     "v4/680e4c57cdc8": norm_emb_bwd_118d525f44e0,
+    "v3/680e4c57cdc8": norm_emb_bwd_118d525f44e0,
+    "v2/680e4c57cdc8": norm_emb_bwd_118d525f44e0,
+    "v1/680e4c57cdc8": norm_emb_bwd_118d525f44e0,
     "v8/f6251e84e3fa": norm_emb_bwd_f6251e84e3fa,
     "v8/12545c1e9b06": emb_rms_12545c1e9b06,
     "v4/6b92d6e665ab": rope_sdpa_6b92d6e665ab,
+    "v5/ca76bd89ec38": rope_sdpa_6b92d6e665ab,
     "v8/f4e9e58fef73": rms_fwd_f4e9e58fef73,
     "v7/f4e9e58fef73": rms_fwd_f4e9e58fef73,
     "v8/4b90e2d83144": rms_fwd_4b90e2d83144,
@@ -370,7 +553,47 @@ PROBLEMS: dict[str, Callable] = {
     "v8/8e33a91b7364": add_rms_unshard_8e33a91b7364,
     "v7/8e33a91b7364": add_rms_unshard_8e33a91b7364,
     "v6/8e33a91b7364": add_rms_unshard_8e33a91b7364,
+    "v5/013a3088b488": add_rms_unshard_t_013a3088b488,
+    "v4/18b859c50de2": add_rms_unshard_tt_18b859c50de2,
+    "v3/18b859c50de2": add_rms_unshard_tt_18b859c50de2,
+    "v2/18b859c50de2": add_rms_unshard_tt_18b859c50de2,
+    "v1/18b859c50de2": add_rms_unshard_tt_18b859c50de2,
+    "v8/94985bdb7630": add_rms_layer_unshard_94985bdb7630,
+    "v8/7815074de963": add_rms_layer_unshard_7815074de963,
+    "v4/84496d824942": rms_fwd_215dd2e6a519,
+    "v3/84496d824942": rms_fwd_215dd2e6a519,
+    "v2/84496d824942": rms_fwd_215dd2e6a519,
+    "v1/84496d824942": rms_fwd_215dd2e6a519,
+    "v4/2a844503364a": rms_fwd_ffn_unshard_2a844503364a,
+    "v3/2a844503364a": rms_fwd_ffn_unshard_2a844503364a,
+    "v2/2a844503364a": rms_fwd_ffn_unshard_2a844503364a,
+    "v1/2a844503364a": rms_fwd_ffn_unshard_2a844503364a,
     "v7/45990c83cfd6": rms_bwd_45990c83cfd6,
+    "v6/822931829090": rms_fwd_bwd3_822931829090,
+    "v5/92ce4a0c7b2c": rms_fwd_bwd3_363b7b58c971,
+    "v4/363b7b58c971": rms_fwd_bwd3_363b7b58c971,
+    "v3/363b7b58c971": rms_fwd_bwd3_363b7b58c971,
+    "v2/363b7b58c971": rms_fwd_bwd3_363b7b58c971,
+    "v1/363b7b58c971": rms_fwd_bwd3_363b7b58c971,
+    "v6/e9198b707240": rms_fwd_bwd2_e9198b707240,
+    "v5/401b52261ef5": rms_fwd_bwd2_84c0a03c4374,
+    "v4/84c0a03c4374": rms_fwd_bwd2_84c0a03c4374,
+    "v3/84c0a03c4374": rms_fwd_bwd2_84c0a03c4374,
+    "v2/84c0a03c4374": rms_fwd_bwd2_84c0a03c4374,
+    "v1/84c0a03c4374": rms_fwd_bwd2_84c0a03c4374,
+    "v6/408ac0979ac5": add_rms_fwd_bwd_408ac0979ac5,
+    "v5/cbfdd7549926": add_rms_fwd_bwd_9c745ea697a7,
+    "v4/9c745ea697a7": add_rms_fwd_bwd_9c745ea697a7,
+    "v3/9c745ea697a7": add_rms_fwd_bwd_9c745ea697a7,
+    "v2/9c745ea697a7": add_rms_fwd_bwd_9c745ea697a7,
+    "v1/9c745ea697a7": add_rms_fwd_bwd_9c745ea697a7,
+    "v6/28b45679fca1": add_rms_bwd_28b45679fca1,
+    "v5/ac7d64b3c769": add_rms_bwd_f7ad66842c19,
+    "v4/f7ad66842c19": add_rms_bwd_f7ad66842c19,
+    "v3/f7ad66842c19": add_rms_bwd_f7ad66842c19,
+    "v2/f7ad66842c19": add_rms_bwd_f7ad66842c19,
+    "v1/f7ad66842c19": add_rms_bwd_f7ad66842c19,
+    "v8/3c6c589cdf81": add2_rms_bwd_3c6c589cdf81,
     "v7/7f544ceb2120": add_rms_bwd_7f544ceb2120,
     "v8/d8f596b3df34": add_rms_bwd_d8f596b3df34,
     "v7/ed20955ec34b": add3_rms_bwd_ed20955ec34b,
@@ -379,6 +602,9 @@ PROBLEMS: dict[str, Callable] = {
     "v6/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v5/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v4/1e49beb8a123": emb_fwd_1e49beb8a123,
+    "v3/1e49beb8a123": emb_fwd_1e49beb8a123,
+    "v2/1e49beb8a123": emb_fwd_1e49beb8a123,
+    "v1/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v7/a12a160cb11b": emb_bwd_a12a160cb11b,
     "v8/c8c60d8f7015": rope_c8c60d8f7015,
     "v6/c8c60d8f7015": rope_c8c60d8f7015,
@@ -392,6 +618,9 @@ PROBLEMS: dict[str, Callable] = {
     "v7/bfe872e373e4": rope_bwd_bfe872e373e4,
     "v7/5c65f62b0422": rope_bwd_5c65f62b0422,
     "v8/7e38211c7f1c": rope_bwd_7e38211c7f1c,
+    "v6/dc55b25cdcb2": rope_bwd_dc55b25cdcb2,
+    "v5/a1bb72d946b0": rope_bwd_qkv_a1318bc813d2,
+    "v4/a1318bc813d2": rope_bwd_qkv_a1318bc813d2,
     "v6/03d64c25b654": rope_bwd_03d64c25b654,
 }
 

@@ -54,6 +54,18 @@ def rms_fwd_ac3fb0b7281f(shard, x):
     return (y2, y2)
 
 
+def rms_fwd_ffn_unshard_2a844503364a(shard, x, s1, s2, s3):
+    """v4/2a844503364a/problem.py:18-74: the norm with the gathered weight,
+    and t() of the three FFN weight clones."""
+    y, _ = F.rmsnorm_fwd(x, _fsdp_weight(shard), 1e-5)
+    y2 = y.view(8192, 4096)
+
+    def clone_view(v, shape):
+        return aten._unsafe_view.default(aten.clone.default(v, memory_format=torch.contiguous_format), shape)
+    return (y2, y2, aten.t.default(clone_view(s1, [14336, 4096])),
+            aten.t.default(clone_view(s2, [14336, 4096])), aten.t.default(clone_view(s3, [4096, 14336])))
+
+
 def add_rms_fwd_7884328a5557(mm_220, add_61, w):
     """v8/7884328a5557/problem.py:17-33: add(add_61, mm_220) then _fused_rms_norm."""
     _, y, _ = F.add_rmsnorm_fwd(add_61, aten._unsafe_view.default(mm_220, [1, 8192, 4096]), w, 1e-5)
@@ -72,6 +84,132 @@ def add_rms_unshard_8e33a91b7364(mm_223, add_62, wait_tensor_969):
     table = aten._unsafe_view.default(aten.clone.default(parts[1], memory_format=torch.contiguous_format),
                                       [128256, 4096])
     return (aten.view.default(y, [8192, 4096]), table)
+
+
+def add_rms_unshard_t_013a3088b488(mm_223, add_62, wait_tensor_969):
+    """v5/013a3088b488/problem.py:15-40: v8/8e33a91b7364's graph, returning
+    t(table) [4096, 128256]."""
+    y, table = add_rms_unshard_8e33a91b7364(mm_223, add_62, wait_tensor_969)
+    return (y, aten.t.default(table))
+
+
+def add_rms_unshard_tt_18b859c50de2(mm_223, add_62, wait_tensor_969):
+    """v4/18b859c50de2/problem.py:12-33 (v1-v3 same id): the same graph with
+    reshape, returning t(t(table)) [128256, 4096]."""
+    y, table = add_rms_unshard_8e33a91b7364(mm_223, add_62, wait_tensor_969)
+    return (y, aten.t.default(aten.t.default(table)))
+
+
+_LAYER_SPLITS = [512, 2097152, 524288, 524288, 2097152, 512, 7340032, 7340032, 7340032]
+_LAYER_VIEWS = [[4096, 4096], [1024, 4096], [1024, 4096], [4096, 4096], [4096], [14336, 4096]]
+
+
+def _add_rms_layer(mm, res, flat):
+    """v8/94985bdb7630/problem.py:14-77: add, split_with_sizes of the
+    [8, 27264000] view, _fused_rms_norm with the split-0 weight, and the
+    clones of splits 1-7 (split 8 unused)."""
+    h = aten.add.Tensor(res, aten._unsafe_view.default(mm, [1, 8192, 4096]))
+    parts = aten.split_with_sizes.default(aten.view.default(flat, [8, -1]), _LAYER_SPLITS, 1)
+    clones = [aten.clone.default(parts[i], memory_format=torch.contiguous_format) for i in range(8)]
+    y, _ = F.rmsnorm_fwd(h, aten._unsafe_view.default(clones[0], [4096]), 1e-5)
+    y2 = aten.view.default(y, [8192, 4096])
+    views = [aten._unsafe_view.default(c, shape) for c, shape in zip(clones[1:7], _LAYER_VIEWS)]
+    return y2, views, clones[7]
+
+
+def add_rms_layer_unshard_94985bdb7630(mm_216, add_60, wait_tensor_966):
+    """v8/94985bdb7630/problem.py:14-79 -> (y x3, splits 1-7 unsharded)."""
+    y, views, last = _add_rms_layer(mm_216, add_60, wait_tensor_966)
+    return (y, y, y, *views, aten._unsafe_view.default(last, [14336, 4096]))
+
+
+def add_rms_layer_unshard_7815074de963(mm_209, add_58, wait_tensor_963):
+    """v8/7815074de963/problem.py:14-77 -> as 94985bdb7630 with split 7 the
+    raw clone [8, 7340032]."""
+    y, views, last = _add_rms_layer(mm_209, add_58, wait_tensor_963)
+    return (y, y, y, *views, last)
+
+
+def _shard_weight(g):
+    """view.dtype -> clone -> _unsafe_view [4096] of an [8, 512] FSDP view."""
+    return aten._unsafe_view.default(aten.clone.default(g, memory_format=torch.contiguous_format),
+                                     [g.numel()])
+
+
+def _norm_then_bwd(h, w, dy, dres):
+    """_fused_rms_norm(h) -> _fused_rms_norm_backward(dy, h, rstd) -> add(dres, dx)
+    -> _to_copy(dw, fp32); returns (y [8192, 4096] view, d, dw fp32)."""
+    y, rstd = F.rmsnorm_fwd(h, w, 1e-5)
+    dx, dw = F.rmsnorm_bwd(dy, h, rstd, w)
+    out = aten.add.Tensor(dres, dx) if dres is not None else dx
+    return aten.view.default(y, [8192, 4096]), out, aten._to_copy.default(dw, dtype=torch.float32)
+
+
+def _mm(t):
+    return aten.view.default(t, [1, 8192, 4096])
+
+
+def rms_fwd_bwd3_822931829090(add_1, w, mm_656, mm_658, mm_660, add_215):
+    """v6/822931829090/problem.py:19-66: fwd, dy = add(add(mm_656, mm_658),
+    mm_660), bwd, add(add_215, dx) -> (y x3, d, dw fp32)."""
+    dy = aten.add.Tensor(aten.add.Tensor(_mm(mm_656), _mm(mm_658)), _mm(mm_660))
+    y, out, dw = _norm_then_bwd(add_1, w, dy, add_215)
+    return (y, y, y, out, dw)
+
+
+def rms_fwd_bwd3_363b7b58c971(getitem_818, add_1, mm_656, mm_658, mm_660, add_215):
+    """v4/363b7b58c971/problem.py:19-75 (v1-v3, v5/92ce4a0c7b2c): the weight
+    cloned out of its [8, 512] view."""
+    return rms_fwd_bwd3_822931829090(add_1, _shard_weight(getitem_818), mm_656, mm_658, mm_660,
+                                     add_215)
+
+
+def rms_fwd_bwd2_e9198b707240(x, w, mm_230, mm_232, getitem_420):
+    """v6/e9198b707240/problem.py:18-56: dy = add(mm_230, mm_232)."""
+    y, out, dw = _norm_then_bwd(x, w, aten.add.Tensor(_mm(mm_230), _mm(mm_232)), getitem_420)
+    return (y, y, out, dw)
+
+
+def rms_fwd_bwd2_84c0a03c4374(getitem_1624, x, mm_230, mm_232, getitem_420):
+    """v4/84c0a03c4374/problem.py:18-65 (v1-v3, v5/401b52261ef5)."""
+    return rms_fwd_bwd2_e9198b707240(x, _shard_weight(getitem_1624), mm_230, mm_232, getitem_420)
+
+
+def add_rms_fwd_bwd_408ac0979ac5(mm_3, embedding, w, mm_664, mm_666, add_218):
+    """v6/408ac0979ac5/problem.py:19-63: h = add(embedding, mm_3)."""
+    h = aten.add.Tensor(embedding, aten._unsafe_view.default(mm_3, [1, 8192, 4096]))
+    y, out, dw = _norm_then_bwd(h, w, aten.add.Tensor(_mm(mm_664), _mm(mm_666)), add_218)
+    return (y, y, out, dw)
+
+
+def add_rms_fwd_bwd_9c745ea697a7(mm_3, embedding, getitem_787, mm_664, mm_666, add_218):
+    """v4/9c745ea697a7/problem.py:19-72 (v1-v3, v5/cbfdd7549926)."""
+    return add_rms_fwd_bwd_408ac0979ac5(mm_3, embedding, _shard_weight(getitem_787), mm_664, mm_666,
+                                        add_218)
+
+
+def add_rms_bwd_28b45679fca1(mm_223, x, mm_226, w):
+    """v6/28b45679fca1/problem.py:17-41: h = add(x, mm_223), bwd of mm_226
+    -> (dh, dw fp32)."""
+    h = aten.add.Tensor(x, aten._unsafe_view.default(mm_223, [1, 8192, 4096]))
+    _, out, dw = _norm_then_bwd(h, w, _mm(mm_226), None)
+    return (out, dw)
+
+
+def add_rms_bwd_f7ad66842c19(mm_223, x, mm_226, wait_tensor_970):
+    """v4/f7ad66842c19/problem.py:17-48 (v1-v3, v5/ac7d64b3c769): the weight
+    is the buffer viewed [8, -1], split [512], viewed [4096]."""
+    parts = aten.split_with_sizes.default(aten.view.default(wait_tensor_970, [8, -1]), [512], 1)
+    return add_rms_bwd_28b45679fca1(mm_223, x, mm_226, aten.view.default(parts[0], [4096]))
+
+
+def add2_rms_bwd_3c6c589cdf81(mm_220, add_61, mm_223, mm_226, w):
+    """v8/3c6c589cdf81/problem.py:18-53: h = add(add(add_61, mm_220), mm_223)
+    -> (dh viewed [8192, 4096], dw fp32)."""
+    h = aten.add.Tensor(aten.add.Tensor(add_61, aten._unsafe_view.default(mm_220, [1, 8192, 4096])),
+                        aten._unsafe_view.default(mm_223, [1, 8192, 4096]))
+    _, out, dw = _norm_then_bwd(h, w, _mm(mm_226), None)
+    return (aten.view.default(out, [8192, 4096]), dw)
 
 
 def rms_bwd_45990c83cfd6(x, w, dy):
@@ -191,6 +329,22 @@ def rope_bwd_03d64c25b654(conj_freqs, g):
     return _rope_bwd(g, aten.clone.default(conj_freqs))
 
 
+def rope_bwd_dc55b25cdcb2(conj_freqs, g):
+    """v6/dc55b25cdcb2/problem.py:15-43: clone(conj) x the q-grad."""
+    return _rope_bwd(g, aten.clone.default(conj_freqs))
+
+
+def rope_bwd_qkv_a1318bc813d2(conj62, conj63, gq, gk, gv):
+    """v4/a1318bc813d2/problem.py:18-85: q x clone(conj63), k x clone(conj62),
+    v passed through; each viewed [S, H*D] and transposed."""
+    dq = _rope_bwd(gq, aten.clone.default(conj63))
+    dk = _rope_bwd(gk, aten.clone.default(conj62))
+    v = aten.transpose.int(gv, 1, 2)
+    _, S, H, D = v.shape
+    dv = aten.reshape.default(aten.reshape.default(v, [1, S, H * D]), [S, H * D])
+    return (aten.t.default(dq), aten.t.default(dk), aten.t.default(dv))
+
+
 SPLITS_873 = [512, 2097152, 524288, 524288, 2097152, 512, 7340032, 7340032, 7340032]
 SHAPES_873 = [[4096, 4096], [1024, 4096], [1024, 4096], [4096, 4096], [4096], [14336, 4096]]
 
@@ -255,9 +409,13 @@ ORACLES = {
     "v6/0b493aad68f0": norm_emb_bwd_0b493aad68f0,
     "v5/118d525f44e0": norm_emb_bwd_118d525f44e0,
     "v4/680e4c57cdc8": norm_emb_bwd_118d525f44e0,
+    "v3/680e4c57cdc8": norm_emb_bwd_118d525f44e0,
+    "v2/680e4c57cdc8": norm_emb_bwd_118d525f44e0,
+    "v1/680e4c57cdc8": norm_emb_bwd_118d525f44e0,
     "v8/f6251e84e3fa": norm_emb_bwd_f6251e84e3fa,
     "v8/12545c1e9b06": emb_rms_12545c1e9b06,
     "v4/6b92d6e665ab": rope_sdpa_6b92d6e665ab,
+    "v5/ca76bd89ec38": rope_sdpa_6b92d6e665ab,
     "v8/f4e9e58fef73": rms_fwd_f4e9e58fef73,
     "v7/f4e9e58fef73": rms_fwd_f4e9e58fef73,
     "v8/4b90e2d83144": rms_fwd_4b90e2d83144,
@@ -270,7 +428,47 @@ ORACLES = {
     "v8/8e33a91b7364": add_rms_unshard_8e33a91b7364,
     "v7/8e33a91b7364": add_rms_unshard_8e33a91b7364,
     "v6/8e33a91b7364": add_rms_unshard_8e33a91b7364,
+    "v5/013a3088b488": add_rms_unshard_t_013a3088b488,
+    "v4/18b859c50de2": add_rms_unshard_tt_18b859c50de2,
+    "v3/18b859c50de2": add_rms_unshard_tt_18b859c50de2,
+    "v2/18b859c50de2": add_rms_unshard_tt_18b859c50de2,
+    "v1/18b859c50de2": add_rms_unshard_tt_18b859c50de2,
+    "v8/94985bdb7630": add_rms_layer_unshard_94985bdb7630,
+    "v8/7815074de963": add_rms_layer_unshard_7815074de963,
+    "v4/84496d824942": rms_fwd_215dd2e6a519,
+    "v3/84496d824942": rms_fwd_215dd2e6a519,
+    "v2/84496d824942": rms_fwd_215dd2e6a519,
+    "v1/84496d824942": rms_fwd_215dd2e6a519,
+    "v4/2a844503364a": rms_fwd_ffn_unshard_2a844503364a,
+    "v3/2a844503364a": rms_fwd_ffn_unshard_2a844503364a,
+    "v2/2a844503364a": rms_fwd_ffn_unshard_2a844503364a,
+    "v1/2a844503364a": rms_fwd_ffn_unshard_2a844503364a,
     "v7/45990c83cfd6": rms_bwd_45990c83cfd6,
+    "v6/822931829090": rms_fwd_bwd3_822931829090,
+    "v5/92ce4a0c7b2c": rms_fwd_bwd3_363b7b58c971,
+    "v4/363b7b58c971": rms_fwd_bwd3_363b7b58c971,
+    "v3/363b7b58c971": rms_fwd_bwd3_363b7b58c971,
+    "v2/363b7b58c971": rms_fwd_bwd3_363b7b58c971,
+    "v1/363b7b58c971": rms_fwd_bwd3_363b7b58c971,
+    "v6/e9198b707240": rms_fwd_bwd2_e9198b707240,
+    "v5/401b52261ef5": rms_fwd_bwd2_84c0a03c4374,
+    "v4/84c0a03c4374": rms_fwd_bwd2_84c0a03c4374,
+    "v3/84c0a03c4374": rms_fwd_bwd2_84c0a03c4374,
+    "v2/84c0a03c4374": rms_fwd_bwd2_84c0a03c4374,
+    "v1/84c0a03c4374": rms_fwd_bwd2_84c0a03c4374,
+    "v6/408ac0979ac5": add_rms_fwd_bwd_408ac0979ac5,
+    "v5/cbfdd7549926": add_rms_fwd_bwd_9c745ea697a7,
+    "v4/9c745ea697a7": add_rms_fwd_bwd_9c745ea697a7,
+    "v3/9c745ea697a7": add_rms_fwd_bwd_9c745ea697a7,
+    "v2/9c745ea697a7": add_rms_fwd_bwd_9c745ea697a7,
+    "v1/9c745ea697a7": add_rms_fwd_bwd_9c745ea697a7,
+    "v6/28b45679fca1": add_rms_bwd_28b45679fca1,
+    "v5/ac7d64b3c769": add_rms_bwd_f7ad66842c19,
+    "v4/f7ad66842c19": add_rms_bwd_f7ad66842c19,
+    "v3/f7ad66842c19": add_rms_bwd_f7ad66842c19,
+    "v2/f7ad66842c19": add_rms_bwd_f7ad66842c19,
+    "v1/f7ad66842c19": add_rms_bwd_f7ad66842c19,
+    "v8/3c6c589cdf81": add2_rms_bwd_3c6c589cdf81,
     "v7/7f544ceb2120": add_rms_bwd_7f544ceb2120,
     "v8/d8f596b3df34": add_rms_bwd_d8f596b3df34,
     "v7/ed20955ec34b": add3_rms_bwd_ed20955ec34b,
@@ -279,6 +477,9 @@ ORACLES = {
     "v6/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v5/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v4/1e49beb8a123": emb_fwd_1e49beb8a123,
+    "v3/1e49beb8a123": emb_fwd_1e49beb8a123,
+    "v2/1e49beb8a123": emb_fwd_1e49beb8a123,
+    "v1/1e49beb8a123": emb_fwd_1e49beb8a123,
     "v7/a12a160cb11b": emb_bwd_a12a160cb11b,
     "v8/c8c60d8f7015": rope_c8c60d8f7015,
     "v6/c8c60d8f7015": rope_c8c60d8f7015,
@@ -292,5 +493,8 @@ ORACLES = {
     "v7/bfe872e373e4": rope_bwd_bfe872e373e4,
     "v7/5c65f62b0422": rope_bwd_5c65f62b0422,
     "v8/7e38211c7f1c": rope_bwd_7e38211c7f1c,
+    "v6/dc55b25cdcb2": rope_bwd_dc55b25cdcb2,
+    "v5/a1bb72d946b0": rope_bwd_qkv_a1318bc813d2,
+    "v4/a1318bc813d2": rope_bwd_qkv_a1318bc813d2,
     "v6/03d64c25b654": rope_bwd_03d64c25b654,
 }

@@ -51,6 +51,35 @@ def assert_bf16_close(actual: torch.Tensor, expected: torch.Tensor, what: str = 
             f"{i}: got {a.flatten()[i].item()} want {e.flatten()[i].item()}")
 
 
+def bf16_ulp(t: torch.Tensor) -> torch.Tensor:
+    """Spacing of bf16 values at |t| (8 significant bits)."""
+    a = t.detach().float().abs().clamp_min(2.0 ** -126)
+    return torch.exp2(torch.floor(torch.log2(a)) - 7)
+
+
+def assert_bf16_sum_close(actual: torch.Tensor, expected: torch.Tensor, addend: torch.Tensor,
+                          what: str = "", max_flips: int = 16):
+    """For outputs bf16(addend + bf16(t)): the intermediate bf16(t) may round
+    the other way when t lands near a rounding boundary (its fp32 value comes
+    from a differently ordered row reduction), which moves the output by one
+    bf16 ulp of |t| -- far above the plain bf16 tolerance when addend and t
+    cancel.  Every element must be within the plain tolerance plus one ulp of
+    |t| = |expected - addend|, and at most `max_flips` may need the ulp."""
+    a = actual.detach().float().cpu()
+    e = expected.detach().float().cpu()
+    t = e - addend.detach().float().cpu().reshape(e.shape)
+    err = (a - e).abs()
+    plain = BF16_ATOL + BF16_RTOL * e.abs()
+    bad = err > plain + bf16_ulp(t)
+    if bad.any():
+        i = int(torch.argmax((err - plain - bf16_ulp(t)).flatten()))
+        raise AssertionError(
+            f"{what}: {int(bad.sum())} of {a.numel()} elements beyond one ulp of the addend-free "
+            f"term; worst at flat {i}: got {a.flatten()[i].item()} want {e.flatten()[i].item()}")
+    flips = int((err > plain).sum())
+    assert flips <= max_flips, f"{what}: {flips} one-ulp roundings of the intermediate (> {max_flips})"
+
+
 def assert_f32_close(actual: torch.Tensor, expected: torch.Tensor, what: str = "",
                      rtol: float = F32_RTOL, atol: float = 0.0):
     a = actual.detach().double().cpu()

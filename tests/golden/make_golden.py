@@ -66,10 +66,16 @@ def sha256(t: torch.Tensor) -> str:
     return hashlib.sha256(c.view(torch.uint8).numpy().tobytes()).hexdigest()
 
 
+MAX_COLS = 65536  # golden rows wider than this keep their first MAX_COLS values
+
+
 def sample_rows(t: torch.Tensor) -> dict:
-    """Rows 0, 1, middle and last of the output flattened to 2-D."""
+    """Rows 0, 1, middle and last of the output flattened to 2-D (the first
+    MAX_COLS columns of wider rows, with "cols" recording the cut)."""
     t2 = t.detach().reshape(-1, t.shape[-1]) if t.dim() > 1 else t.detach().reshape(1, -1)
     idx = sorted({0, min(1, t2.shape[0] - 1), t2.shape[0] // 2, t2.shape[0] - 1})
+    if t2.shape[1] > MAX_COLS:
+        return {"rows": idx, "cols": MAX_COLS, "values": t2[idx, :MAX_COLS].clone()}
     return {"rows": idx, "values": t2[idx].clone()}
 
 

@@ -62,6 +62,28 @@ def test_invalid_arguments_rejected_on_host():
     assert lib.frag_rope(t, 1, 1, 1, 128, null, 0, 0, 0, null, 0, 0, 1e4, 7, 0, null) == 1  # bad layout
     assert lib.frag_rope(t, 3, 1, 1, 128, null, 0, 0, 0, null, 0, 0, 1e4, 0, 0, null) == 1  # > 2 tensors
     assert lib.frag_rope(t, 1, 1, 1, 127, null, 0, 0, 0, null, 0, 0, 1e4, 0, 0, null) == 2  # odd D
+    fb = lib.frag_rmsnorm_fwd_bwd
+    assert fb(null, null, 8, null, null, null, null, null, null, null, null, null, null, 4, 8, 1e-5,
+              null, 0, null) == 1                                                  # x3 without x2
+    assert fb(null, null, null, null, null, null, null, null, null, null, null, null, null, -1, 8,
+              1e-5, null, 0, null) == 1
+    assert fb(null, null, null, null, null, null, null, null, null, null, null, null, null, 4, 8,
+              1e-5, null, 0, null) == 1                                            # null x, dy
+    assert fb(null, null, null, null, null, null, null, null, null, null, null, null, null, 0, 8,
+              1e-5, null, 0, null) == 0                                            # empty, no dw
+    seg = _lib.CopySegment
+    segs = (seg * 17)()
+    assert lib.frag_copy_rows_grouped(segs, 0, null) == 0                       # nothing to copy
+    assert lib.frag_copy_rows_grouped(segs, 17, null) == 1                      # > 16 segments
+    assert lib.frag_copy_rows_grouped(segs, -1, null) == 1
+    assert lib.frag_copy_rows_grouped(None, 1, null) == 1
+    assert lib.frag_copy_rows_grouped(segs, 16, null) == 0                      # all empty
+    bad = (seg * 2)(seg(None, None, 0, 0, 0, 64), seg(None, None, 64, 64, -1, 64))
+    assert lib.frag_copy_rows_grouped(bad, 2, null) == 1                        # negative rows
+    bad = (seg * 1)(seg(None, None, 64, 64, 2, 64))
+    assert lib.frag_copy_rows_grouped(bad, 1, null) == 1                        # null pointers
+    bad = (seg * 1)(seg(4096, 8192, 16, 64, 2, 64))
+    assert lib.frag_copy_rows_grouped(bad, 1, null) == 2                        # rows overlap
 
 
 def test_fraggerror_message():

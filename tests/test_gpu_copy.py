@@ -34,3 +34,49 @@ def test_copy_rows_empty_and_errors():
     assert ops.copy_rows(e).shape == (0, 16)
     with pytest.raises(ValueError):
         ops.copy_rows(torch.zeros(4, 4, device="cuda").t())   # columns not contiguous
+
+
+def _layer_buffer(world, splits, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return torch.randn(world * sum(splits), generator=g, device="cuda").to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("world,splits", [
+    (8, [512, 2097152, 524288, 524288, 2097152, 512, 7340032, 7340032]),   # one decoder layer
+    (8, [512, 65667072]),                                                  # norm weight + table
+    (3, [8, 1000, 24, 4096, 40]),
+    (2, [8] * 16),                                                        # the segment limit
+    (5, [0, 64, 0, 128]),                                                 # empty splits
+])
+def test_copy_rows_grouped_splits(world, splits):
+    flat = _layer_buffer(world, splits, world * 31 + len(splits))
+    parts = torch.split(flat.view(world, -1), splits, dim=1)
+    outs = ops.copy_rows_grouped(parts)
+    assert len(outs) == len(parts)
+    for o, v in zip(outs, parts):
+        assert o.is_contiguous() and o.shape == v.shape
+        assert torch.equal(o, v.contiguous())
+
+
+def test_copy_rows_grouped_into_outs_and_unaligned():
+    flat = _layer_buffer(4, [40, 24, 8], 5)
+    parts = torch.split(flat.view(4, -1), [40, 24, 8], dim=1)
+    outs = [torch.full(p.shape, 7.0, device="cuda", dtype=torch.bfloat16) for p in parts]
+    got = ops.copy_rows_grouped(parts, [outs[0], None, outs[2]])
+    assert got[0] is outs[0] and got[2] is outs[2]
+    for o, v in zip(got, parts):
+        assert torch.equal(o, v.contiguous())
+    # rows 2 bytes off 16-byte alignment: one frag_copy_rows per segment
+    odd = torch.split(flat.view(4, -1)[:, 1:], [39, 24, 8], dim=1)
+    for o, v in zip(ops.copy_rows_grouped(odd), odd):
+        assert torch.equal(o, v.contiguous())
+
+
+def test_copy_rows_grouped_errors():
+    flat = _layer_buffer(2, [8] * 17, 9)
+    parts = torch.split(flat.view(2, -1), [8] * 17, dim=1)
+    with pytest.raises(ValueError):
+        ops.copy_rows_grouped(parts)                       # 17 > 16 segments
+    with pytest.raises(ValueError):
+        ops.copy_rows_grouped(parts[:2], [None])           # outs length
+    assert ops.copy_rows_grouped([]) == []
