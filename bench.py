@@ -58,7 +58,8 @@ DOMINANT = "C4B"  # largest share of the step; its main kernel is the roofline k
 #   C2S  FSDP table unshard + add/RMSNorm (one grouped copy, then the norm)
 #   C2L  FSDP decoder-layer unshard (8 splits) + add/RMSNorm
 #   C1R  RMSNorm forward recomputed in its backward, one pass (C1U: two calls)
-NEXT = ["C2N", "C3S", "C2C", "C2U", "C2S", "C2L", "C1R", "C1U"]
+#   C3X  complex64 RoPE of the v1/v2 snapshots (fp32 in and out)
+NEXT = ["C2N", "C3S", "C2C", "C2U", "C2S", "C2L", "C1R", "C1U", "C3X"]
 
 
 # ------------------------------------------------------------------ helpers
@@ -445,6 +446,23 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
                                                         inverse=inv), h)
         return f
 
+    def mk_c3x():
+        # the v1/v2 snapshots' RoPE: complex64 q [1, 8192, 32, 64] and
+        # k [1, 8192, 8, 64] times freqs_cis[pos] (v2/075cb40f3d5d shapes)
+        S, Hq, Hk, D2 = 8192, 32, 8, 64
+        g = torch.Generator(device=dev).manual_seed(seed0 + 60)
+        q = torch.randn((1, S, Hq, D2), dtype=torch.complex64, device=dev, generator=g)
+        k = torch.randn((1, S, Hk, D2), dtype=torch.complex64, device=dev, generator=g)
+        freqs = torch.randn((S, D2), dtype=torch.complex64, device=dev, generator=g)
+        pos = torch.randint(0, S, (1, S), dtype=torch.int32, device=dev, generator=g)
+        oq, ok = torch.empty_like(q), torch.empty_like(k)
+        nb = 2 * S * (Hq + Hk) * D2 * 8 + S * 4 + S * D2 * 8
+        f = Frag("C3X", "complex64 RoPE q[1,8192,32,64] k[1,8192,8,64] x freqs_cis[pos]", S, nb,
+                 [("rope_complex", lambda: ops.rope_complex(q, k, pos, freqs, out_q=oq, out_k=ok))])
+        f.host = dict(q=q, k=k)
+        f.e2e = lambda h: _e2e_call(lambda xs: ops.rope_complex(xs["q"], xs["k"], pos, freqs), h)
+        return f
+
     def mk_c4f():
         c = C4
         w = cf.rmsnorm_weight(c.N, device=dev, seed=seed0 + 20)
@@ -595,7 +613,7 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
                           "FSDP layer unshard (8 splits) + add/RMSNorm [8192,4096]")
 
     builders = {"C2N": mk_c2n, "C3S": mk_c3s, "C2S": mk_c2s, "C2L": mk_c2l,
-                "C1R": lambda: mk_fwd_bwd("C1R"), "C1U": lambda: mk_fwd_bwd("C1U"), "C2C": lambda: mk_chain("C2C"),
+                "C1R": lambda: mk_fwd_bwd("C1R"), "C3X": mk_c3x, "C1U": lambda: mk_fwd_bwd("C1U"), "C2C": lambda: mk_chain("C2C"),
                 "C2U": lambda: mk_chain("C2U"), "C0F": mk_c0f, "C1B": lambda: mk_rms_bwd("C1B", C1, False, 3, False),
                 "C2F": lambda: mk_c2("C2F"), "C2B": lambda: mk_c2("C2B"),
                 "C3F": lambda: mk_c3("C3F"), "C3B": lambda: mk_c3("C3B"),
@@ -632,7 +650,8 @@ def _e2e_call(fn, host, pipe=None):
     outs = outs if isinstance(outs, (tuple, list)) else (outs,)
     h2d = sum(v.numel() * v.element_size() for v in host["in"].values())
     d2h = 0
-    tensors = [o for o in outs if isinstance(o, torch.Tensor)]
+    flat = [t for o in outs for t in (o if isinstance(o, (tuple, list)) else (o,))]
+    tensors = [o for o in flat if isinstance(o, torch.Tensor)]
     if pipe is not None:
         d2h_s.wait_stream(cur)
     for i, o in enumerate(tensors):

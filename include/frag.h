@@ -68,6 +68,9 @@ enum frag_rope_layout { FRAG_ROPE_NEOX = 0, FRAG_ROPE_INTERLEAVED = 1 };
 /* RoPE output element types (frag_rope_tensor.out_dtype). */
 enum frag_rope_out { FRAG_ROPE_OUT_BF16 = 0, FRAG_ROPE_OUT_F32 = 1 };
 
+/* RoPE input element types (frag_rope_tensor.in_dtype). */
+enum frag_rope_in { FRAG_ROPE_IN_BF16 = 0, FRAG_ROPE_IN_F32 = 1 };
+
 /* Position tensor dtypes for RoPE. NONE means position = token index s. */
 enum frag_pos_dtype { FRAG_POS_NONE = 0, FRAG_POS_I32 = 1, FRAG_POS_I64 = 2 };
 
@@ -366,6 +369,12 @@ typedef struct frag_rope_tensor {
    * (1): out is fp32, not rounded (v7/0f38bc55457c/problem.py:10-40 returns
    * q that way); out strides are in elements of out's type. */
   int32_t out_dtype;
+  /* FRAG_ROPE_IN_BF16 (0): x is bf16; FRAG_ROPE_IN_F32 (1): x is fp32, a
+   * complex64 tensor viewed as (re, im) pairs -- the v1/v2 snapshots' complex
+   * multiply (v2/075cb40f3d5d/problem.py:15-27, v2/9cd8f72e74ce/problem.py:13-16)
+   * -- which needs FRAG_ROPE_INTERLEAVED, out_dtype FRAG_ROPE_OUT_F32 and the
+   * same in_dtype for every tensor of the call; x strides in elements of x. */
+  int32_t in_dtype;
 } frag_rope_tensor;
 
 FRAG_API int frag_rope(const frag_rope_tensor* tensors, int num_tensors, int64_t B,

@@ -27,6 +27,8 @@ FRAG_DEVFLAG_INDEX_OOB = 1
 FRAG_DEVFLAG_WAIT_TIMEOUT = 2
 FRAG_ROPE_OUT_BF16 = 0
 FRAG_ROPE_OUT_F32 = 1
+FRAG_ROPE_IN_BF16 = 0
+FRAG_ROPE_IN_F32 = 1
 FRAG_ROPE_NEOX = 0
 FRAG_ROPE_INTERLEAVED = 1
 FRAG_POS_NONE = 0
@@ -61,6 +63,7 @@ class RopeTensor(C.Structure):
         ("out_stride_s", _i64),
         ("out_stride_h", _i64),
         ("out_dtype", C.c_int32),  # FRAG_ROPE_OUT_BF16 / FRAG_ROPE_OUT_F32
+        ("in_dtype", C.c_int32),   # FRAG_ROPE_IN_BF16 / FRAG_ROPE_IN_F32
     ]
 
 

@@ -10,7 +10,10 @@
 //   angle_j = float(pos) * inv_freq[j],  inv_freq[j] = theta^(-2j/D)
 // with the accurate sincosf, so no cache tensor is read from HBM.
 // The backward is the same rotation by the conjugate (v6/03d64c25b654/problem.py:12-43
-// multiplies the incoming gradient by conj(freqs_cis)).
+// multiplies the incoming gradient by conj(freqs_cis)).  The v1/v2 snapshots
+// multiply complex64 tensors directly (v2/075cb40f3d5d/problem.py:15-27:
+// view_as_complex inputs times freqs_cis[pos], complex64 out): fp32 input
+// with the interleaved layout, fp32 output, no rounding anywhere.
 //
 // Vector path: one warp per token; D/16 lanes per head.  Lane j owns the two
 // 16-byte chunks at element offsets 8j and D/2 + 8j of every head, so each
@@ -30,11 +33,12 @@ namespace {
 constexpr int kMaxHalf = 256;  // D <= 512
 
 struct RopeT {
-  const uint16_t* x;
-  void* out;  // bf16, or fp32 with of32
+  const void* x;  // bf16, or fp32 with if32
+  void* out;      // bf16, or fp32 with of32
   int H;
   int64_t xsb, xss, xsh, osb, oss, osh;  // elements of x's / out's type
   int of32;
+  int if32;
 };
 
 struct RopeP {
@@ -62,11 +66,9 @@ __device__ __forceinline__ int64_t load_pos(const RopeP& p, int64_t b, int64_t s
 }
 
 template <bool NEOX>
-__device__ __forceinline__ void rotate_f(const uint4& a, const uint4& c, const float (&cs)[8],
-                                         const float (&sn)[8], float (&ra)[8], float (&rc)[8]) {
-  float fa[8], fc[8];
-  unpack8(a, fa);
-  unpack8(c, fc);
+__device__ __forceinline__ void rotate_vals(const float (&fa)[8], const float (&fc)[8],
+                                            const float (&cs)[8], const float (&sn)[8],
+                                            float (&ra)[8], float (&rc)[8]) {
   if (NEOX) {
     // a = x[8j..8j+8), c = x[D/2+8j..): pair i is (fa[i], fc[i]).
 #pragma unroll
@@ -89,6 +91,22 @@ __device__ __forceinline__ void rotate_f(const uint4& a, const uint4& c, const f
 }
 
 template <bool NEOX>
+__device__ __forceinline__ void rotate_f(const uint4& a, const uint4& c, const float (&cs)[8],
+                                         const float (&sn)[8], float (&ra)[8], float (&rc)[8]) {
+  float fa[8], fc[8];
+  unpack8(a, fa);
+  unpack8(c, fc);
+  rotate_vals<NEOX>(fa, fc, cs, sn, ra, rc);
+}
+
+// 8 fp32 values (32 bytes) from x at element offset `off`.
+__device__ __forceinline__ void load_f32x8(const float* x, float (&v)[8]) {
+  const float4 a = ld_stream_f4(x), b = ld_stream_f4(x + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <bool NEOX>
 __device__ __forceinline__ void rotate(const uint4& a, const uint4& c, const float (&cs)[8],
                                        const float (&sn)[8], uint4& oa, uint4& oc) {
   float ra[8], rc[8];
@@ -104,7 +122,9 @@ __device__ __forceinline__ void store_f32x8(const RopeT& T, int64_t off, const f
   o[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
-template <int LPH, bool NEOX, bool TABLE, bool ANYF32>
+// INF32: fp32 inputs (and outputs); a lane's two groups of 8 elements sit at
+// the same element offsets as the bf16 chunks, 32 bytes each.
+template <int LPH, bool NEOX, bool TABLE, bool ANYF32, bool INF32 = false>
 __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
   __shared__ float sfreq[kMaxHalf];
   const int half = p.D >> 1;
@@ -164,8 +184,34 @@ __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
   for (int ti = 0; ti < 2; ++ti) {
     if (ti >= p.nt) break;
     const RopeT& T = p.t[ti];
-    const uint16_t* xb = T.x + b * T.xsb + s * T.xss;
     const int64_t ob = b * T.osb + s * T.oss;
+    if constexpr (INF32) {
+      const float* xf = static_cast<const float*>(T.x) + b * T.xsb + s * T.xss;
+      constexpr int UF = 2;  // 32 fp32 values of loads in flight per lane
+      for (int h0 = hs; h0 < T.H; h0 += HPI * UF) {
+        float fa[UF][8], fc[UF][8];
+#pragma unroll
+        for (int u = 0; u < UF; ++u) {
+          const int h = h0 + u * HPI;
+          if (h < T.H) {
+            load_f32x8(xf + h * T.xsh + oa, fa[u]);
+            load_f32x8(xf + h * T.xsh + oc, fc[u]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < UF; ++u) {
+          const int h = h0 + u * HPI;
+          if (h < T.H) {
+            float ra[8], rc[8];
+            rotate_vals<NEOX>(fa[u], fc[u], cs, sn, ra, rc);
+            store_f32x8(T, ob + h * T.osh + oa, ra);
+            store_f32x8(T, ob + h * T.osh + oc, rc);
+          }
+        }
+      }
+      continue;
+    }
+    const uint16_t* xb = static_cast<const uint16_t*>(T.x) + b * T.xsb + s * T.xss;
     for (int h0 = hs; h0 < T.H; h0 += HPI * UNR) {
       uint4 va[UNR], vc[UNR];
 #pragma unroll
@@ -214,7 +260,8 @@ __global__ void __launch_bounds__(256) rope_generic(const RopeP p) {
   for (int ti = 0; ti < 2; ++ti) {
     if (ti >= p.nt) break;
     const RopeT& T = p.t[ti];
-    const uint16_t* xb = T.x + b * T.xsb + s * T.xss;
+    const uint16_t* xb = static_cast<const uint16_t*>(T.x) + b * T.xsb + s * T.xss;
+    const float* xf = static_cast<const float*>(T.x) + b * T.xsb + s * T.xss;
     const int64_t ob = b * T.osb + s * T.oss;
     for (int64_t q = threadIdx.x; q < static_cast<int64_t>(T.H) * half; q += blockDim.x) {
       const int h = static_cast<int>(q / half), jj = static_cast<int>(q - static_cast<int64_t>(h) * half);
@@ -231,8 +278,8 @@ __global__ void __launch_bounds__(256) rope_generic(const RopeP p) {
       sv *= p.sign;
       const int ia = NEOX ? jj : 2 * jj;
       const int ic = NEOX ? jj + half : 2 * jj + 1;
-      const float a = bf16_to_f(xb[h * T.xsh + ia]);
-      const float c = bf16_to_f(xb[h * T.xsh + ic]);
+      const float a = T.if32 ? xf[h * T.xsh + ia] : bf16_to_f(xb[h * T.xsh + ia]);
+      const float c = T.if32 ? xf[h * T.xsh + ic] : bf16_to_f(xb[h * T.xsh + ic]);
       const float ra = a * cv - c * sv;
       const float rc = NEOX ? c * cv + a * sv : a * sv + c * cv;
       if (T.of32) {
@@ -246,16 +293,16 @@ __global__ void __launch_bounds__(256) rope_generic(const RopeP p) {
   }
 }
 
-template <bool NEOX, bool TABLE, bool ANYF32>
+template <bool NEOX, bool TABLE, bool ANYF32, bool INF32 = false>
 int launch_rope_vec(const RopeP& p, cudaStream_t s) {
   const dim3 grid(static_cast<unsigned>(ceil_div(p.B * p.S, 8)));
   switch (p.D / 16) {
-    case 1: rope_vec<1, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
-    case 2: rope_vec<2, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
-    case 4: rope_vec<4, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
-    case 8: rope_vec<8, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
-    case 16: rope_vec<16, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
-    case 32: rope_vec<32, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 1: rope_vec<1, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
+    case 2: rope_vec<2, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
+    case 4: rope_vec<4, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
+    case 8: rope_vec<8, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
+    case 16: rope_vec<16, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
+    case 32: rope_vec<32, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
     default: return FRAG_ERR_SHAPE;
   }
   return check_launch();
@@ -265,7 +312,12 @@ template <bool NEOX, bool TABLE>
 int launch_rope_t(const RopeP& p, bool vec, cudaStream_t s) {
   if (vec) {
     // fp32 outputs get their own instantiation: the bf16-only kernel keeps
-    // its register count (and CTAs per SM)
+    // its register count (and CTAs per SM); fp32 inputs (all tensors of the
+    // call) another, interleaved pairs only (complex64 tensors)
+    if (p.t[0].if32) {
+      if constexpr (NEOX) return FRAG_ERR_SHAPE;
+      else return launch_rope_vec<NEOX, TABLE, true, true>(p, s);
+    }
     const bool anyf32 = p.t[0].of32 || (p.nt > 1 && p.t[1].of32);
     return anyf32 ? launch_rope_vec<NEOX, TABLE, true>(p, s) : launch_rope_vec<NEOX, TABLE, false>(p, s);
   }
@@ -319,15 +371,22 @@ extern "C" int frag_rope(const frag_rope_tensor* tensors, int num_tensors, int64
 
   bool vec = D % 16 == 0 && (D / 16) <= 32 && (32 % (D / 16)) == 0;
   if (freqs) vec = vec && aligned16(freqs) && freqs_stride % 2 == 0;
-  p.t[1] = RopeT{nullptr, nullptr, 0, 0, 0, 0, 0, 0, 0, 0};
+  p.t[1] = RopeT{nullptr, nullptr, 0, 0, 0, 0, 0, 0, 0, 0, 0};
   for (int i = 0; i < num_tensors; ++i) {
     const frag_rope_tensor& t = tensors[i];
     if (t.H < 0 || t.H > 0x7fffffffLL) return FRAG_ERR_SHAPE;
     if (t.H > 0 && (!t.x || !t.out)) return FRAG_ERR_INVALID_ARG;
     if (t.out_dtype != FRAG_ROPE_OUT_BF16 && t.out_dtype != FRAG_ROPE_OUT_F32) return FRAG_ERR_INVALID_ARG;
-    p.t[i] = RopeT{static_cast<const uint16_t*>(t.x), t.out, static_cast<int>(t.H), t.x_stride_b,
+    if (t.in_dtype != FRAG_ROPE_IN_BF16 && t.in_dtype != FRAG_ROPE_IN_F32) return FRAG_ERR_INVALID_ARG;
+    // fp32 (complex64) inputs: fp32 outputs, the interleaved layout, and the
+    // same input type for every tensor of the call
+    if (t.in_dtype == FRAG_ROPE_IN_F32 &&
+        (t.out_dtype != FRAG_ROPE_OUT_F32 || layout != FRAG_ROPE_INTERLEAVED))
+      return FRAG_ERR_INVALID_ARG;
+    if (i > 0 && t.in_dtype != tensors[0].in_dtype) return FRAG_ERR_INVALID_ARG;
+    p.t[i] = RopeT{t.x, t.out, static_cast<int>(t.H), t.x_stride_b,
                    t.x_stride_s, t.x_stride_h, t.out_stride_b, t.out_stride_s, t.out_stride_h,
-                   t.out_dtype == FRAG_ROPE_OUT_F32 ? 1 : 0};
+                   t.out_dtype == FRAG_ROPE_OUT_F32 ? 1 : 0, t.in_dtype == FRAG_ROPE_IN_F32 ? 1 : 0};
     const int64_t st[6] = {t.x_stride_b, t.x_stride_s, t.x_stride_h,
                            t.out_stride_b, t.out_stride_s, t.out_stride_h};
     for (int k = 0; k < 6; ++k) vec = vec && (st[k] % 8 == 0);

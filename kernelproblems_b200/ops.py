@@ -37,6 +37,7 @@ __all__ = [
     "copy_rows",
     "copy_rows_grouped",
     "rope",
+    "rope_complex",
     "check_status",
     "reset_status",
 ]
@@ -549,8 +550,34 @@ def _rope_desc(x: torch.Tensor, out: torch.Tensor, name: str) -> _lib.RopeTensor
         raise TypeError(f"{name}: the output must be bf16 or float32 on {x.device}")
     B, S, H, D = x.shape
     odt = _lib.FRAG_ROPE_OUT_F32 if out.dtype == torch.float32 else _lib.FRAG_ROPE_OUT_BF16
+    idt = _lib.FRAG_ROPE_IN_F32 if x.dtype == torch.float32 else _lib.FRAG_ROPE_IN_BF16
+    if idt == _lib.FRAG_ROPE_IN_F32 and odt != _lib.FRAG_ROPE_OUT_F32:
+        raise TypeError(f"{name}: a float32 input needs a float32 output")
     return _lib.RopeTensor(x.data_ptr(), out.data_ptr(), H, x.stride(0), x.stride(1), x.stride(2),
-                           out.stride(0), out.stride(1), out.stride(2), odt)
+                           out.stride(0), out.stride(1), out.stride(2), odt, idt)
+
+
+def rope_complex(q: torch.Tensor, k: torch.Tensor | None, positions: torch.Tensor | None,
+                 freqs: torch.Tensor, *, inverse: bool = False, out_q: torch.Tensor | None = None,
+                 out_k: torch.Tensor | None = None):
+    """The complex multiply of the v1/v2 snapshots: q (and k) complex64
+    [B, S, H, D/2] times freqs[positions] (complex64 [P, D/2]; positions None
+    = s), complex64 results (new, or the given out_q / out_k), fp32
+    arithmetic throughout -> (out_q, out_k)."""
+    def real(t, name):
+        if not isinstance(t, torch.Tensor) or t.dtype != torch.complex64 or t.dim() != 4:
+            raise TypeError(f"{name} must be a complex64 [B, S, H, D/2] tensor")
+        if t.stride(-1) != 1:
+            raise ValueError(f"{name}: the last dimension must be contiguous")
+        return torch.view_as_real(t).flatten(-2)
+    oq = torch.empty(q.shape, dtype=torch.complex64, device=q.device) if out_q is None else out_q
+    ok = None
+    if k is not None:
+        ok = torch.empty(k.shape, dtype=torch.complex64, device=k.device) if out_k is None else out_k
+    rope(real(q, "q"), None if k is None else real(k, "k"), positions, theta=None, freqs=freqs,
+         layout="interleaved", inverse=inverse, out_q=real(oq, "out_q"),
+         out_k=None if ok is None else real(ok, "out_k"))
+    return oq, ok
 
 
 def _new_out(x: torch.Tensor, out_layout: str) -> torch.Tensor:
@@ -578,9 +605,16 @@ def rope(q: torch.Tensor, k: torch.Tensor | None = None, positions: torch.Tensor
     storage order attention kernels read (the transpose is fused into the
     stores; the returned tensors are [B, S, H, D] views of that storage, so
     `.transpose(1, 2)` gives contiguous [B, H, S, D]).  An out_q / out_k of
-    dtype float32 receives the rotated values unrounded."""
-    _need(q, "q", torch.bfloat16)
+    dtype float32 receives the rotated values unrounded.  float32 q and k
+    (complex64 tensors viewed as (re, im) pairs, see rope_complex) take the
+    interleaved layout and float32 outputs."""
+    if not isinstance(q, torch.Tensor) or q.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("q must be a bfloat16 or float32 torch.Tensor")
+    if not q.is_cuda:
+        raise ValueError("q must be a CUDA tensor")
     dev = q.device
+    if q.dtype == torch.float32 and layout != "interleaved":
+        raise ValueError("float32 (complex) inputs take the interleaved layout")
     if layout not in _LAYOUTS:
         raise ValueError(f"layout must be one of {sorted(_LAYOUTS)}")
     B, S, Hq, D = q.shape
@@ -588,7 +622,7 @@ def rope(q: torch.Tensor, k: torch.Tensor | None = None, positions: torch.Tensor
     descs = [_rope_desc(q, oq, "q")]
     ok = None
     if k is not None:
-        _need(k, "k", torch.bfloat16, dev)
+        _need(k, "k", q.dtype, dev)
         if k.shape[0] != B or k.shape[1] != S or k.shape[3] != D:
             raise ValueError(f"k {tuple(k.shape)} does not match q {tuple(q.shape)}")
         ok = _new_out(k, out_layout) if out_k is None else out_k

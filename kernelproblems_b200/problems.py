@@ -459,6 +459,47 @@ def rope_bwd_qkv_a1318bc813d2(_conj_62, _conj_63, getitem_641, getitem_642, geti
     return (dq.t(), dk.t(), dv.t())
 
 
+def rope_c64_075cb40f3d5d(arg586_1, arg582_1, view_as_complex_60, view_as_complex_61):
+    """v2/075cb40f3d5d/problem.py:17-29 (v1 same id): complex64 q and k
+    times freqs_cis[pos] (index -> mul -> mul), complex64 out."""
+    S = view_as_complex_60.shape[1]
+    return ops.rope_complex(view_as_complex_60, view_as_complex_61, arg586_1.view(1, S), arg582_1)
+
+
+def _rope_c64_conj(conj, x):
+    # x * clone(conj), conj [1, S, 1, D/2] read as a table indexed by s
+    S = x.shape[1]
+    oq, _ = ops.rope_complex(x, None, None, conj.reshape(S, -1))
+    return oq
+
+
+def rope_c64_bwd_9cd8f72e74ce(_conj_63, view_as_complex_127):
+    """v2/9cd8f72e74ce/problem.py:15-18 (v1 same id): complex64 q-grad
+    [1, S, 32, 64] times clone(_conj_63) -> complex64."""
+    return _rope_c64_conj(_conj_63, view_as_complex_127)
+
+
+def rope_c64_bwd_f23f9bb4567a(_conj_62, view_as_complex_126):
+    """v2/f23f9bb4567a/problem.py:15-18 (v1 same id): the k-grad
+    [1, S, 8, 64] times clone(_conj_62)."""
+    return _rope_c64_conj(_conj_62, view_as_complex_126)
+
+
+def rope_c64_layers_d7efc428b2f5(arg586_1, arg582_1, *qk):
+    """v2/d7efc428b2f5/problem.py:81-509 (v1 same id): the complex RoPE of
+    33 (q, k) pairs (the layers' recomputed projections), each times
+    freqs_cis[pos] -> 66 complex64 outputs in input order; one launch per
+    pair."""
+    if len(qk) % 2:
+        raise ValueError("expected (q, k) pairs")
+    S = qk[0].shape[1]
+    pos = arg586_1.view(1, S)
+    outs = []
+    for i in range(0, len(qk), 2):
+        outs.extend(ops.rope_complex(qk[i], qk[i + 1], pos, arg582_1))
+    return tuple(outs)
+
+
 # ------------------------------------------ fused chains across the path
 
 def emb_rms_12545c1e9b06(wait_tensor_871, arg583_1, wait_tensor_873):
@@ -618,6 +659,14 @@ PROBLEMS: dict[str, Callable] = {
     "v7/bfe872e373e4": rope_bwd_bfe872e373e4,
     "v7/5c65f62b0422": rope_bwd_5c65f62b0422,
     "v8/7e38211c7f1c": rope_bwd_7e38211c7f1c,
+    "v2/075cb40f3d5d": rope_c64_075cb40f3d5d,
+    "v1/075cb40f3d5d": rope_c64_075cb40f3d5d,
+    "v2/9cd8f72e74ce": rope_c64_bwd_9cd8f72e74ce,
+    "v1/9cd8f72e74ce": rope_c64_bwd_9cd8f72e74ce,
+    "v2/f23f9bb4567a": rope_c64_bwd_f23f9bb4567a,
+    "v1/f23f9bb4567a": rope_c64_bwd_f23f9bb4567a,
+    "v2/d7efc428b2f5": rope_c64_layers_d7efc428b2f5,
+    "v1/d7efc428b2f5": rope_c64_layers_d7efc428b2f5,
     "v6/dc55b25cdcb2": rope_bwd_dc55b25cdcb2,
     "v5/a1bb72d946b0": rope_bwd_qkv_a1318bc813d2,
     "v4/a1318bc813d2": rope_bwd_qkv_a1318bc813d2,

@@ -345,6 +345,38 @@ def rope_bwd_qkv_a1318bc813d2(conj62, conj63, gq, gk, gv):
     return (aten.t.default(dq), aten.t.default(dk), aten.t.default(dv))
 
 
+def _freqs_at(pos, freqs):
+    # squeeze -> index -> view [1, S, 1, D/2]
+    f = aten.index.Tensor(freqs, [aten.squeeze.dim(pos, 0)])
+    return aten.view.default(f, [1, f.shape[0], 1, f.shape[1]])
+
+
+def rope_c64_075cb40f3d5d(pos, freqs, q, k):
+    """v2/075cb40f3d5d/problem.py:17-29: mul(q, f), mul(k, f) in complex64."""
+    f = _freqs_at(pos, freqs)
+    return (aten.mul.Tensor(q, f), aten.mul.Tensor(k, f))
+
+
+def rope_c64_bwd_9cd8f72e74ce(conj, x):
+    """v2/9cd8f72e74ce/problem.py:15-18: mul(x, clone(conj))."""
+    return aten.mul.Tensor(x, aten.clone.default(conj))
+
+
+def rope_c64_bwd_f23f9bb4567a(conj, x):
+    """v2/f23f9bb4567a/problem.py:15-18."""
+    return aten.mul.Tensor(x, aten.clone.default(conj))
+
+
+def rope_c64_layers_d7efc428b2f5(pos, freqs, *qk):
+    """v2/d7efc428b2f5/problem.py:81-509: per (q, k) pair, index the table
+    again and multiply both."""
+    outs = []
+    for i in range(0, len(qk), 2):
+        f = _freqs_at(pos, freqs)
+        outs += [aten.mul.Tensor(qk[i], f), aten.mul.Tensor(qk[i + 1], f)]
+    return tuple(outs)
+
+
 SPLITS_873 = [512, 2097152, 524288, 524288, 2097152, 512, 7340032, 7340032, 7340032]
 SHAPES_873 = [[4096, 4096], [1024, 4096], [1024, 4096], [4096, 4096], [4096], [14336, 4096]]
 
@@ -493,6 +525,14 @@ ORACLES = {
     "v7/bfe872e373e4": rope_bwd_bfe872e373e4,
     "v7/5c65f62b0422": rope_bwd_5c65f62b0422,
     "v8/7e38211c7f1c": rope_bwd_7e38211c7f1c,
+    "v2/075cb40f3d5d": rope_c64_075cb40f3d5d,
+    "v1/075cb40f3d5d": rope_c64_075cb40f3d5d,
+    "v2/9cd8f72e74ce": rope_c64_bwd_9cd8f72e74ce,
+    "v1/9cd8f72e74ce": rope_c64_bwd_9cd8f72e74ce,
+    "v2/f23f9bb4567a": rope_c64_bwd_f23f9bb4567a,
+    "v1/f23f9bb4567a": rope_c64_bwd_f23f9bb4567a,
+    "v2/d7efc428b2f5": rope_c64_layers_d7efc428b2f5,
+    "v1/d7efc428b2f5": rope_c64_layers_d7efc428b2f5,
     "v6/dc55b25cdcb2": rope_bwd_dc55b25cdcb2,
     "v5/a1bb72d946b0": rope_bwd_qkv_a1318bc813d2,
     "v4/a1318bc813d2": rope_bwd_qkv_a1318bc813d2,

@@ -62,6 +62,15 @@ def test_invalid_arguments_rejected_on_host():
     assert lib.frag_rope(t, 1, 1, 1, 128, null, 0, 0, 0, null, 0, 0, 1e4, 7, 0, null) == 1  # bad layout
     assert lib.frag_rope(t, 3, 1, 1, 128, null, 0, 0, 0, null, 0, 0, 1e4, 0, 0, null) == 1  # > 2 tensors
     assert lib.frag_rope(t, 1, 1, 1, 127, null, 0, 0, 0, null, 0, 0, 1e4, 0, 0, null) == 2  # odd D
+    T = _lib.RopeTensor
+    for descs, layout in (([T(16, 32, 1, 0, 0, 0, 0, 0, 0, 0, 1)], 1),    # fp32 in, bf16 out
+                          ([T(16, 32, 1, 0, 0, 0, 0, 0, 0, 1, 1)], 0),    # fp32 in, neox
+                          ([T(16, 32, 1, 0, 0, 0, 0, 0, 0, 1, 1),
+                            T(16, 32, 1, 0, 0, 0, 0, 0, 0, 0, 0)], 1),    # mixed input types
+                          ([T(16, 32, 1, 0, 0, 0, 0, 0, 0, 0, 5)], 1)):   # unknown in_dtype
+        arr = (T * len(descs))(*descs)
+        assert lib.frag_rope(arr, len(descs), 1, 1, 128, null, 0, 0, 0, null, 0, 0, 1e4, layout, 0,
+                             null) == 1
     fb = lib.frag_rmsnorm_fwd_bwd
     assert fb(null, null, 8, null, null, null, null, null, null, null, null, null, null, 4, 8, 1e-5,
               null, 0, null) == 1                                                  # x3 without x2

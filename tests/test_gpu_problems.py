@@ -208,6 +208,12 @@ def test_problem_drop_in(fixture):
             # contracted into FMAs, so a few ulps of the products' magnitude
             assert_f32_close(oc, e, "q (fp32)", rtol=1e-5, atol=1e-5)
             assert_f32_close(o2[rows], g["values"], "q golden rows", rtol=1e-5, atol=1e-5)
+        elif o.dtype == torch.complex64:
+            # complex64 products, fp32 throughout: a few ulps (FMA contraction)
+            assert_f32_close(torch.view_as_real(oc), torch.view_as_real(e), f"output {i} (complex64)",
+                             rtol=1e-5, atol=1e-5)
+            assert_f32_close(torch.view_as_real(o2[rows]), torch.view_as_real(g["values"]),
+                             f"output {i} golden rows", rtol=1e-5, atol=1e-5)
         elif o.dtype == torch.float32:  # saved rstd
             assert_f32_close(oc, e, f"output {i} (fp32)")
             assert_f32_close(o2[rows], g["values"], f"output {i} golden rows")

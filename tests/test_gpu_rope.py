@@ -105,3 +105,41 @@ def test_rope_fp32_output_is_unrounded(D):
     assert oq.dtype == torch.float32 and ok.dtype == torch.bfloat16
     assert_f32_close(oq.cpu(), ref_q, "fp32 q", rtol=1e-5, atol=1e-5)
     assert_bf16_close(ok.cpu(), ora.rope_interleaved(k, f), "bf16 k")
+
+
+@pytest.mark.parametrize("D2,Hq,Hk", [(64, 32, 8), (12, 3, 2), (8, 4, 0)])
+def test_rope_complex64(D2, Hq, Hk):
+    """ops.rope_complex (fp32 inputs, the v1/v2 snapshots' complex multiply):
+    complex64 q, k times freqs[pos], fp32 throughout; D/2 = 12 takes the
+    generic kernel."""
+    from conftest import assert_f32_close
+    S = 48
+    g = torch.Generator().manual_seed(D2 + Hq)
+    q = torch.randn(1, S, Hq, D2, generator=g, dtype=torch.complex64)
+    k = torch.randn(1, S, Hk, D2, generator=g, dtype=torch.complex64) if Hk else None
+    freqs = torch.randn(100, D2, generator=g, dtype=torch.complex64)
+    pos = torch.randint(0, 100, (1, S), generator=g, dtype=torch.int32)
+    oq, ok = ops.rope_complex(q.cuda(), None if k is None else k.cuda(), pos.cuda(), freqs.cuda())
+    f = freqs[pos[0].long()].view(1, S, 1, D2)
+    assert oq.dtype == torch.complex64 and oq.shape == q.shape
+    assert_f32_close(torch.view_as_real(oq.cpu()), torch.view_as_real(q * f), "q", rtol=1e-5, atol=1e-5)
+    if k is not None:
+        assert_f32_close(torch.view_as_real(ok.cpu()), torch.view_as_real(k * f), "k", rtol=1e-5,
+                         atol=1e-5)
+    # the backward: multiply by the conjugate table
+    gq, _ = ops.rope_complex(oq, None, pos.cuda(), freqs.cuda(), inverse=True)
+    assert_f32_close(torch.view_as_real(gq.cpu()), torch.view_as_real(q * f * f.conj()), "q round trip",
+                     rtol=1e-4, atol=1e-4)
+
+
+def test_rope_complex64_errors():
+    q = torch.zeros(1, 4, 2, 64, dtype=torch.complex64, device="cuda")
+    qr = torch.view_as_real(q).flatten(-2)
+    f = torch.zeros(4, 64, dtype=torch.complex64, device="cuda")
+    with pytest.raises(ValueError):
+        ops.rope(qr, None, None, freqs=f, layout="neox", out_q=torch.empty_like(qr))
+    with pytest.raises(TypeError):
+        ops.rope(qr, None, None, freqs=f, layout="interleaved",
+                 out_q=torch.empty(qr.shape, dtype=torch.bfloat16, device="cuda"))
+    with pytest.raises(TypeError):
+        ops.rope_complex(qr, None, None, f)          # not complex
