@@ -71,6 +71,9 @@ enum frag_rope_out { FRAG_ROPE_OUT_BF16 = 0, FRAG_ROPE_OUT_F32 = 1 };
 /* RoPE input element types (frag_rope_tensor.in_dtype). */
 enum frag_rope_in { FRAG_ROPE_IN_BF16 = 0, FRAG_ROPE_IN_F32 = 1 };
 
+/* Element types of frag_convert_rows. */
+enum frag_dtype { FRAG_DT_BF16 = 0, FRAG_DT_F32 = 1 };
+
 /* Position tensor dtypes for RoPE. NONE means position = token index s. */
 enum frag_pos_dtype { FRAG_POS_NONE = 0, FRAG_POS_I32 = 1, FRAG_POS_I64 = 2 };
 
@@ -332,6 +335,26 @@ typedef struct frag_copy_segment {
 } frag_copy_segment;
 
 FRAG_API int frag_copy_rows_grouped(const frag_copy_segment* segs, int32_t n, frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Element type conversion of row-strided rows: dst row r (and dst2 row r when
+ * dst2 is non-NULL) <- src row r converted from src_dtype to dst_dtype
+ * (FRAG_DT_BF16 / FRAG_DT_F32), `cols` elements per row, rows src_stride /
+ * dst_stride elements (of each side's type) apart; fp32 -> bf16 rounds to
+ * nearest even, bf16 -> fp32 is exact.  No destination may overlap the
+ * source or the other destination.  Replaces the aten._to_copy casts around
+ * the complex RoPE multiply of the v1-v3 snapshots:
+ *   v2/dcf660c50ef3/problem.py:14-37 and v2/5d51b24b8d83/problem.py:14-37
+ *     (q / k projections widened to fp32, twice: dst and dst2),
+ *   v2/b3f1b1135abc/problem.py:16-43 (the SDPA-layout q / k gradients),
+ *   v2/d800447a68f6/problem.py:14-26, v2/3e3eb10963d7/problem.py:14-26,
+ *   v2/db48e1361360/problem.py:14-22, v2/b508c9141fed/problem.py:14-22
+ *     (view_as_real results rounded back to bf16),
+ * and their v1 / v3 snapshots.
+ * ------------------------------------------------------------------------- */
+FRAG_API int frag_convert_rows(const void* src, int32_t src_dtype, int64_t src_stride, void* dst,
+                               void* dst2, int32_t dst_dtype, int64_t dst_stride, int64_t rows,
+                               int64_t cols, frag_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Rotary position embedding on up to two tensors (q and k) in one launch.

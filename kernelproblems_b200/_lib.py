@@ -27,6 +27,8 @@ FRAG_DEVFLAG_INDEX_OOB = 1
 FRAG_DEVFLAG_WAIT_TIMEOUT = 2
 FRAG_ROPE_OUT_BF16 = 0
 FRAG_ROPE_OUT_F32 = 1
+FRAG_DT_BF16 = 0
+FRAG_DT_F32 = 1
 FRAG_ROPE_IN_BF16 = 0
 FRAG_ROPE_IN_F32 = 1
 FRAG_ROPE_NEOX = 0
@@ -110,6 +112,7 @@ SIGNATURES: dict[str, tuple] = {
     "frag_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64]),
     "frag_copy_rows": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp]),
     "frag_copy_rows_grouped": (_int, [C.POINTER(CopySegment), C.c_int32, _vp]),
+    "frag_convert_rows": (_int, [_vp, C.c_int32, _i64, _vp, _vp, C.c_int32, _i64, _i64, _i64, _vp]),
     "frag_selftest_bounded_wait": (_int, [_i64, _vp]),
     "frag_rmsnorm_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "frag_rmsnorm_embedding_bwd": (

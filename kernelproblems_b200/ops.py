@@ -36,6 +36,7 @@ __all__ = [
     "rmsnorm_embedding_bwd",
     "copy_rows",
     "copy_rows_grouped",
+    "convert",
     "rope",
     "rope_complex",
     "check_status",
@@ -532,6 +533,37 @@ def copy_rows_grouped(srcs, outs=None) -> list[torch.Tensor]:
     with _on_device(dev):
         _lib.call("frag_copy_rows_grouped", segs, len(srcs), _stream(dev))
     return outs
+
+
+_DT = {torch.bfloat16: _lib.FRAG_DT_BF16, torch.float32: _lib.FRAG_DT_F32}
+
+
+def convert(src: torch.Tensor, dtype: torch.dtype, copies: int = 1):
+    """bf16 <-> fp32 element type conversion (frag_convert_rows): a new
+    contiguous tensor of src's shape in `dtype` (fp32 -> bf16 rounds to
+    nearest even), or a tuple of `copies` (1 or 2) such tensors written by
+    one pass.  src may be any view whose last dimension is contiguous and
+    whose leading dimensions collapse into one row stride."""
+    if not isinstance(src, torch.Tensor) or src.dtype not in _DT or dtype not in _DT:
+        raise TypeError("convert takes bfloat16 / float32 tensors and dtypes")
+    if not src.is_cuda:
+        raise ValueError("src must be a CUDA tensor")
+    if copies not in (1, 2):
+        raise ValueError("copies must be 1 or 2")
+    cols = src.shape[-1] if src.dim() else 1
+    try:
+        rows2d = src.view(-1, cols) if src.dim() else src.view(1, 1)
+    except RuntimeError:
+        raise ValueError("src's leading dimensions must collapse into one row stride") from None
+    if cols > 1 and rows2d.stride(1) != 1:
+        raise ValueError("src's last dimension must be contiguous")
+    outs = [torch.empty(src.shape, dtype=dtype, device=src.device) for _ in range(copies)]
+    rows = rows2d.shape[0]
+    with _on_device(src.device):
+        _lib.call("frag_convert_rows", _ptr(rows2d), _DT[src.dtype], rows2d.stride(0) if rows > 1 else cols,
+                  _ptr(outs[0]), _ptr(outs[1]) if copies == 2 else None, _DT[dtype], cols, rows, cols,
+                  _stream(src.device))
+    return outs[0] if copies == 1 else tuple(outs)
 
 
 # ------------------------------------------------------------------- RoPE

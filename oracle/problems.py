@@ -377,6 +377,44 @@ def rope_c64_layers_d7efc428b2f5(pos, freqs, *qk):
     return tuple(outs)
 
 
+def cast_f32_twice_dcf660c50ef3(mm):
+    """v2/dcf660c50ef3/problem.py:14-37: reshape [1, S, -1, 128] -> _to_copy
+    fp32 -> reshape [.., -1, 2], done twice."""
+    S = mm.shape[0]
+    outs = []
+    for _ in range(2):
+        x = aten.reshape.default(aten.reshape.default(mm, [1, S, mm.shape[1]]), [1, S, -1, 128])
+        f = aten._to_copy.default(x, dtype=torch.float32)
+        outs.append(aten.reshape.default(f, [1, S, f.shape[2], -1, 2]))
+    return tuple(outs)
+
+
+def cast_bwd_qkv_b3f1b1135abc(gq, gk, gv):
+    """v2/b3f1b1135abc/problem.py:16-43."""
+    def widen(g):
+        f = aten._to_copy.default(aten.transpose.int(g, 1, 2), dtype=torch.float32)
+        return aten.reshape.default(f, [1, f.shape[1], f.shape[2], 64, 2])
+    v = aten.transpose.int(gv, 1, 2)
+    _, S, H, D = v.shape
+    dv = aten.reshape.default(aten.reshape.default(v, [1, S, H * D]), [S, H * D])
+    return (widen(gq), widen(gk), aten.t.default(dv))
+
+
+def cast_bf16_t_d800447a68f6(x):
+    """v2/d800447a68f6/problem.py:14-26."""
+    _, S, H, P, _ = x.shape
+    y = aten._to_copy.default(aten.reshape.default(x, [1, S, H, 2 * P]), dtype=torch.bfloat16)
+    y = aten.reshape.default(aten.reshape.default(y, [1, S, H * 2 * P]), [S, H * 2 * P])
+    return aten.t.default(y)
+
+
+def cast_bf16_bhsd_db48e1361360(x):
+    """v2/db48e1361360/problem.py:14-22."""
+    _, S, H, P, _ = x.shape
+    y = aten._to_copy.default(aten.reshape.default(x, [1, S, H, 2 * P]), dtype=torch.bfloat16)
+    return aten.transpose.int(y, 1, 2)
+
+
 SPLITS_873 = [512, 2097152, 524288, 524288, 2097152, 512, 7340032, 7340032, 7340032]
 SHAPES_873 = [[4096, 4096], [1024, 4096], [1024, 4096], [4096, 4096], [4096], [14336, 4096]]
 
@@ -525,6 +563,27 @@ ORACLES = {
     "v7/bfe872e373e4": rope_bwd_bfe872e373e4,
     "v7/5c65f62b0422": rope_bwd_5c65f62b0422,
     "v8/7e38211c7f1c": rope_bwd_7e38211c7f1c,
+    "v3/dcf660c50ef3": cast_f32_twice_dcf660c50ef3,
+    "v2/dcf660c50ef3": cast_f32_twice_dcf660c50ef3,
+    "v1/dcf660c50ef3": cast_f32_twice_dcf660c50ef3,
+    "v3/5d51b24b8d83": cast_f32_twice_dcf660c50ef3,
+    "v2/5d51b24b8d83": cast_f32_twice_dcf660c50ef3,
+    "v1/5d51b24b8d83": cast_f32_twice_dcf660c50ef3,
+    "v3/b3f1b1135abc": cast_bwd_qkv_b3f1b1135abc,
+    "v2/b3f1b1135abc": cast_bwd_qkv_b3f1b1135abc,
+    "v1/b3f1b1135abc": cast_bwd_qkv_b3f1b1135abc,
+    "v3/d800447a68f6": cast_bf16_t_d800447a68f6,
+    "v2/d800447a68f6": cast_bf16_t_d800447a68f6,
+    "v1/d800447a68f6": cast_bf16_t_d800447a68f6,
+    "v3/3e3eb10963d7": cast_bf16_t_d800447a68f6,
+    "v2/3e3eb10963d7": cast_bf16_t_d800447a68f6,
+    "v1/3e3eb10963d7": cast_bf16_t_d800447a68f6,
+    "v3/db48e1361360": cast_bf16_bhsd_db48e1361360,
+    "v2/db48e1361360": cast_bf16_bhsd_db48e1361360,
+    "v1/db48e1361360": cast_bf16_bhsd_db48e1361360,
+    "v3/b508c9141fed": cast_bf16_bhsd_db48e1361360,
+    "v2/b508c9141fed": cast_bf16_bhsd_db48e1361360,
+    "v1/b508c9141fed": cast_bf16_bhsd_db48e1361360,
     "v2/075cb40f3d5d": rope_c64_075cb40f3d5d,
     "v1/075cb40f3d5d": rope_c64_075cb40f3d5d,
     "v2/9cd8f72e74ce": rope_c64_bwd_9cd8f72e74ce,

@@ -84,6 +84,11 @@ def load_problem(ref_root: Path, key: str) -> types.ModuleType:
     src = src.replace("device(type='cuda', index=0)", "device(type='cpu')")
     src = re.sub(r"device='cuda(:0)?'", "device='cpu'", src)
     mod = types.ModuleType(key.replace("/", "_"))
+    # Some v1 graphs (v1/b3f1b1135abc, v1/3e3eb10963d7, v1/b508c9141fed,
+    # v1/d800447a68f6, v1/db48e1361360) call device(...) without the
+    # `from torch import device` their v2 snapshots have, so as shipped they
+    # raise NameError; the name is supplied here, as v2 imports it.
+    mod.__dict__["device"] = torch.device
     exec(compile(src, str(ref_root / key / "problem.py"), "exec"), mod.__dict__)
     return mod
 

@@ -80,6 +80,12 @@ def test_invalid_arguments_rejected_on_host():
               1e-5, null, 0, null) == 1                                            # null x, dy
     assert fb(null, null, null, null, null, null, null, null, null, null, null, null, null, 0, 8,
               1e-5, null, 0, null) == 0                                            # empty, no dw
+    cv = lib.frag_convert_rows
+    assert cv(null, 0, 8, null, null, 1, 8, 4, 8, null) == 1     # null src / dst
+    assert cv(16, 2, 8, 32, null, 1, 8, 4, 8, null) == 1         # unknown dtype
+    assert cv(16, 0, 4, 32, null, 1, 8, 4, 8, null) == 2         # source rows overlap
+    assert cv(null, 0, 8, null, null, 1, 8, 0, 8, null) == 0     # empty
+    assert cv(16, 0, 8, 32, null, 1, 8, -1, 8, null) == 1
     seg = _lib.CopySegment
     segs = (seg * 17)()
     assert lib.frag_copy_rows_grouped(segs, 0, null) == 0                       # nothing to copy

@@ -80,3 +80,36 @@ def test_copy_rows_grouped_errors():
     with pytest.raises(ValueError):
         ops.copy_rows_grouped(parts[:2], [None])           # outs length
     assert ops.copy_rows_grouped([]) == []
+
+
+@pytest.mark.parametrize("shape,src_dt,dst_dt", [
+    ((1, 8192, 32, 128), torch.bfloat16, torch.float32),    # the RoPE input widening
+    ((1, 8192, 8, 128), torch.float32, torch.bfloat16),     # the RoPE result rounding
+    ((37, 1000), torch.float32, torch.bfloat16),
+    ((5, 13), torch.bfloat16, torch.float32),                # cols % 8 != 0: element kernel
+    ((64, 256), torch.float32, torch.float32),
+])
+def test_convert(shape, src_dt, dst_dt):
+    g = torch.Generator(device="cuda").manual_seed(len(shape) * 100 + shape[-1])
+    x = (torch.randn(shape, generator=g, device="cuda") * 3).to(src_dt)
+    y = ops.convert(x, dst_dt)
+    assert y.dtype == dst_dt and y.shape == x.shape and y.is_contiguous()
+    assert torch.equal(y, x.to(dst_dt)), "conversion must match torch's _to_copy bit for bit"
+
+
+def test_convert_strided_two_copies_and_errors():
+    g = torch.Generator(device="cuda").manual_seed(7)
+    base = torch.randn(64, 160, generator=g, device="cuda")
+    rows = base[:, 16:144]                                    # rows 160 apart, 128 wide
+    a, b = ops.convert(rows, torch.bfloat16, copies=2)
+    assert a.data_ptr() != b.data_ptr()
+    assert torch.equal(a, rows.to(torch.bfloat16)) and torch.equal(b, a)
+    odd = base[:, 1:130]                                      # unaligned rows: element kernel
+    assert torch.equal(ops.convert(odd, torch.bfloat16), odd.to(torch.bfloat16))
+    t = torch.randn(8, 4, 16, generator=g, device="cuda").transpose(0, 1)   # [4, 8, 16] view
+    with pytest.raises(ValueError):
+        ops.convert(t, torch.bfloat16)                        # rows do not collapse
+    with pytest.raises(TypeError):
+        ops.convert(base.to(torch.float16), torch.float32)
+    with pytest.raises(ValueError):
+        ops.convert(base, torch.float32, copies=3)
