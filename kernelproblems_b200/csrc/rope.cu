@@ -122,32 +122,17 @@ __device__ __forceinline__ void store_f32x8(const RopeT& T, int64_t off, const f
   o[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
-// INF32: fp32 inputs (and outputs); a lane's two groups of 8 elements sit at
-// the same element offsets as the bf16 chunks, 32 bytes each.
-template <int LPH, bool NEOX, bool TABLE, bool ANYF32, bool INF32 = false>
-__global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
-  __shared__ float sfreq[kMaxHalf];
-  const int half = p.D >> 1;
-  if (!TABLE)
-    for (int i = threadIdx.x; i < half; i += blockDim.x) sfreq[i] = p.inv_freq[i];
-  __syncthreads();
-  constexpr int HPI = 32 / LPH;  // heads per warp iteration
-  constexpr int UNR = 4;
-  const int lane = threadIdx.x & 31;
-  const int64_t tok = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (tok >= p.B * p.S) return;
-  const int64_t b = tok / p.S, s = tok - b * p.S;
-  const int64_t pos = load_pos(p, b, s);
-  const int j = lane % LPH, hs = lane / LPH;
-  // A position outside the table is an input error (the reference's
-  // freqs_cis[pos] raises): flag it and rotate by nothing instead of
-  // reading outside the table.
+// The 8 (cos, sin) of lane j's rotation pairs at position `pos` (the
+// conjugate for the inverse); a position outside the table is flagged and
+// rotates by nothing instead of reading outside it.
+template <bool NEOX, bool TABLE>
+__device__ __forceinline__ void lane_freqs(const RopeP& p, int64_t pos, int j, int half,
+                                           const float* sfreq, bool report, float (&cs)[8],
+                                           float (&sn)[8]) {
   const bool bad = TABLE && (pos < 0 || pos >= p.frows);
-  if (bad && lane == 0 && p.err) atomicOr(p.err, FRAG_DEVFLAG_INDEX_OOB);
-
+  if (bad && report && p.err) atomicOr(p.err, FRAG_DEVFLAG_INDEX_OOB);
   // Frequency index of pair i (0..7) of this lane.
   auto fidx = [&](int i) { return NEOX ? 8 * j + i : (i < 4 ? 4 * j + i : (half >> 1) + 4 * j + i - 4); };
-  float cs[8], sn[8];
   if (bad) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -176,6 +161,25 @@ __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
       sn[i] = sv * p.sign;
     }
   }
+}
+
+template <int LPH, bool NEOX, bool TABLE, bool ANYF32>
+__global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
+  __shared__ float sfreq[kMaxHalf];
+  const int half = p.D >> 1;
+  if (!TABLE)
+    for (int i = threadIdx.x; i < half; i += blockDim.x) sfreq[i] = p.inv_freq[i];
+  __syncthreads();
+  constexpr int HPI = 32 / LPH;  // heads per warp iteration
+  constexpr int UNR = 4;
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (tok >= p.B * p.S) return;
+  const int64_t b = tok / p.S, s = tok - b * p.S;
+  const int64_t pos = load_pos(p, b, s);
+  const int j = lane % LPH, hs = lane / LPH;
+  float cs[8], sn[8];
+  lane_freqs<NEOX, TABLE>(p, pos, j, half, sfreq, lane == 0, cs, sn);
 
   // Element offsets of this lane's two 16-byte chunks within a head.
   const int oa = 8 * j;
@@ -185,32 +189,6 @@ __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
     if (ti >= p.nt) break;
     const RopeT& T = p.t[ti];
     const int64_t ob = b * T.osb + s * T.oss;
-    if constexpr (INF32) {
-      const float* xf = static_cast<const float*>(T.x) + b * T.xsb + s * T.xss;
-      constexpr int UF = 2;  // 32 fp32 values of loads in flight per lane
-      for (int h0 = hs; h0 < T.H; h0 += HPI * UF) {
-        float fa[UF][8], fc[UF][8];
-#pragma unroll
-        for (int u = 0; u < UF; ++u) {
-          const int h = h0 + u * HPI;
-          if (h < T.H) {
-            load_f32x8(xf + h * T.xsh + oa, fa[u]);
-            load_f32x8(xf + h * T.xsh + oc, fc[u]);
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < UF; ++u) {
-          const int h = h0 + u * HPI;
-          if (h < T.H) {
-            float ra[8], rc[8];
-            rotate_vals<NEOX>(fa[u], fc[u], cs, sn, ra, rc);
-            store_f32x8(T, ob + h * T.osh + oa, ra);
-            store_f32x8(T, ob + h * T.osh + oc, rc);
-          }
-        }
-      }
-      continue;
-    }
     const uint16_t* xb = static_cast<const uint16_t*>(T.x) + b * T.xsb + s * T.xss;
     for (int h0 = hs; h0 < T.H; h0 += HPI * UNR) {
       uint4 va[UNR], vc[UNR];
@@ -239,6 +217,60 @@ __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
           }
         }
       }
+    }
+  }
+}
+
+// fp32 (complex64) inputs and outputs, interleaved pairs: one warp per unit
+// = (token, group of HG heads of one tensor), so a short sequence still
+// fills every resident warp several times over (a persistent grid walking
+// the units measured slower).  A lane's two groups of 8 elements sit at the
+// bf16 chunks' element offsets, 32 bytes each.
+template <int LPH, bool TABLE>
+__global__ void __launch_bounds__(256) rope_vec_f32(const RopeP p, int units_q, int units_k) {
+  __shared__ float sfreq[kMaxHalf];
+  const int half = p.D >> 1;
+  if (!TABLE)
+    for (int i = threadIdx.x; i < half; i += blockDim.x) sfreq[i] = p.inv_freq[i];
+  __syncthreads();
+  constexpr int HPI = 32 / LPH;  // heads per warp iteration
+  constexpr int UF = 2;          // iterations per unit, loads issued together
+  constexpr int HG = HPI * UF;   // heads per unit
+  const int U = units_q + units_k;
+  const int lane = threadIdx.x & 31;
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= p.B * p.S * U) return;
+  const int64_t tok = w / U;
+  const int u = static_cast<int>(w - tok * U);
+  const int ti = u < units_q ? 0 : 1;
+  const int hbase = (ti == 0 ? u : u - units_q) * HG;
+  const int64_t b = tok / p.S, s = tok - b * p.S;
+  const int64_t pos = load_pos(p, b, s);
+  const int j = lane % LPH, hs = lane / LPH;
+  float cs[8], sn[8];
+  // one report per token: the unit holding its first q heads
+  lane_freqs<false, TABLE>(p, pos, j, half, sfreq, lane == 0 && u == 0, cs, sn);
+  const RopeT& T = p.t[ti];
+  const float* xf = static_cast<const float*>(T.x) + b * T.xsb + s * T.xss;
+  const int64_t ob = b * T.osb + s * T.oss;
+  const int oa = 8 * j, oc = half + 8 * j;
+  float fa[UF][8], fc[UF][8];
+#pragma unroll
+  for (int k = 0; k < UF; ++k) {
+    const int h = hbase + hs + k * HPI;
+    if (h < T.H) {
+      load_f32x8(xf + h * T.xsh + oa, fa[k]);
+      load_f32x8(xf + h * T.xsh + oc, fc[k]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < UF; ++k) {
+    const int h = hbase + hs + k * HPI;
+    if (h < T.H) {
+      float ra[8], rc[8];
+      rotate_vals<false>(fa[k], fc[k], cs, sn, ra, rc);
+      store_f32x8(T, ob + h * T.osh + oa, ra);
+      store_f32x8(T, ob + h * T.osh + oc, rc);
     }
   }
 }
@@ -293,19 +325,44 @@ __global__ void __launch_bounds__(256) rope_generic(const RopeP p) {
   }
 }
 
-template <bool NEOX, bool TABLE, bool ANYF32, bool INF32 = false>
+template <bool NEOX, bool TABLE, bool ANYF32>
 int launch_rope_vec(const RopeP& p, cudaStream_t s) {
   const dim3 grid(static_cast<unsigned>(ceil_div(p.B * p.S, 8)));
   switch (p.D / 16) {
-    case 1: rope_vec<1, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
-    case 2: rope_vec<2, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
-    case 4: rope_vec<4, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
-    case 8: rope_vec<8, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
-    case 16: rope_vec<16, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
-    case 32: rope_vec<32, NEOX, TABLE, ANYF32, INF32><<<grid, 256, 0, s>>>(p); break;
+    case 1: rope_vec<1, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 2: rope_vec<2, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 4: rope_vec<4, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 8: rope_vec<8, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 16: rope_vec<16, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
+    case 32: rope_vec<32, NEOX, TABLE, ANYF32><<<grid, 256, 0, s>>>(p); break;
     default: return FRAG_ERR_SHAPE;
   }
   return check_launch();
+}
+
+template <int LPH, bool TABLE>
+int launch_rope_f32_lph(const RopeP& p, cudaStream_t s) {
+  constexpr int HG = 2 * (32 / LPH);
+  const int uq = static_cast<int>(ceil_div(p.t[0].H, HG));
+  const int uk = p.nt > 1 ? static_cast<int>(ceil_div(p.t[1].H, HG)) : 0;
+  const int64_t warps = p.B * p.S * (uq + uk);
+  if (warps == 0) return FRAG_OK;
+  if (ceil_div(warps, 8) > 0x7fffffffLL) return FRAG_ERR_SHAPE;
+  rope_vec_f32<LPH, TABLE><<<static_cast<unsigned>(ceil_div(warps, 8)), 256, 0, s>>>(p, uq, uk);
+  return check_launch();
+}
+
+template <bool TABLE>
+int launch_rope_f32(const RopeP& p, cudaStream_t s) {
+  switch (p.D / 16) {
+    case 1: return launch_rope_f32_lph<1, TABLE>(p, s);
+    case 2: return launch_rope_f32_lph<2, TABLE>(p, s);
+    case 4: return launch_rope_f32_lph<4, TABLE>(p, s);
+    case 8: return launch_rope_f32_lph<8, TABLE>(p, s);
+    case 16: return launch_rope_f32_lph<16, TABLE>(p, s);
+    case 32: return launch_rope_f32_lph<32, TABLE>(p, s);
+    default: return FRAG_ERR_SHAPE;
+  }
 }
 
 template <bool NEOX, bool TABLE>
@@ -316,7 +373,7 @@ int launch_rope_t(const RopeP& p, bool vec, cudaStream_t s) {
     // call) another, interleaved pairs only (complex64 tensors)
     if (p.t[0].if32) {
       if constexpr (NEOX) return FRAG_ERR_SHAPE;
-      else return launch_rope_vec<NEOX, TABLE, true, true>(p, s);
+      else return launch_rope_f32<TABLE>(p, s);
     }
     const bool anyf32 = p.t[0].of32 || (p.nt > 1 && p.t[1].of32);
     return anyf32 ? launch_rope_vec<NEOX, TABLE, true>(p, s) : launch_rope_vec<NEOX, TABLE, false>(p, s);

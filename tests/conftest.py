@@ -51,6 +51,13 @@ def assert_bf16_close(actual: torch.Tensor, expected: torch.Tensor, what: str = 
             f"{i}: got {a.flatten()[i].item()} want {e.flatten()[i].item()}")
 
 
+# Problems whose graph repeats one op chain over many input groups: the
+# oracle is pinned on the first groups (inputs, outputs) -- the same aten ops
+# as the rest -- instead of generating every input (v1-v2/d7efc428b2f5: 33
+# (q, k) pairs, 5.5 GB of complex64 inputs).
+ORACLE_PREFIX = {"d7efc428b2f5": (6, 4)}
+
+
 def bf16_ulp(t: torch.Tensor) -> torch.Tensor:
     """Spacing of bf16 values at |t| (8 significant bits)."""
     a = t.detach().float().abs().clamp_min(2.0 ** -126)

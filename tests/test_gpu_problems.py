@@ -16,6 +16,7 @@ from pathlib import Path
 import pytest
 import torch
 
+from conftest import ORACLE_PREFIX as PREFIX
 from conftest import assert_bf16_close, assert_bf16_sum_close, assert_f32_close
 from kernelproblems_b200.problems import PROBLEMS
 from oracle import fragments as F
@@ -147,7 +148,10 @@ def _dw_f64(key, cpu_in):
 def test_problem_drop_in(fixture):
     fx = torch.load(fixture, weights_only=False)
     key = fx["problem"]
-    cpu_in = make_inputs(fx["inputs"])
+    # the oracle runs on the first input groups of PREFIX problems (the same
+    # ops as the rest); every output is still checked against its golden rows
+    ni, no = PREFIX.get(key.split("/")[1], (len(fx["inputs"]), len(fx["outputs"])))
+    cpu_in = make_inputs(fx["inputs"][:ni])
     gpu_in = make_inputs(fx["inputs"], device="cuda")
     outs = PROBLEMS[key](*gpu_in)
     outs = outs if isinstance(outs, (tuple, list)) else (outs,)
@@ -155,13 +159,19 @@ def test_problem_drop_in(fixture):
     _check_structure(outs, fx)
     ref = ORACLES[key](*cpu_in)
     ref = ref if isinstance(ref, (tuple, list)) else (ref,)
+    assert len(ref) == no
+    ref = tuple(ref) + (None,) * (len(outs) - no)
     for i, (o, e, g) in enumerate(zip(outs, ref, fx["outputs"])):
         oc = o.cpu()
         rows = torch.tensor(g["rows"])
         o2 = oc.reshape(-1, oc.shape[-1]) if oc.dim() > 1 else oc.reshape(1, -1)
         # golden rows wider than the fixture's column cap are stored truncated
         o2 = o2[:, :g["cols"]] if "cols" in g else o2
-        if key in EXACT:
+        if e is None:  # beyond the oracle's prefix: the reference's golden rows
+            assert o.dtype == torch.complex64
+            assert_f32_close(torch.view_as_real(o2[rows]), torch.view_as_real(g["values"]),
+                             f"output {i} golden rows", rtol=1e-5, atol=1e-5)
+        elif key in EXACT:
             assert torch.equal(oc, e), "gathers and casts must be bit exact"
             assert torch.equal(o2[rows], g["values"]), "golden rows"
         elif i in UNSHARD.get(key, ()):
