@@ -96,6 +96,24 @@ def add_rmsnorm_bwd_dp(dy: torch.Tensor, dh: torch.Tensor, h: torch.Tensor,
                           dres=dh, bwd_fn=bwd_fn, reduce_fn=reduce_fn)
 
 
+def rmsnorm_fwd_bwd_dp(x: torch.Tensor, weight: torch.Tensor, dy: torch.Tensor, *,
+                       x2: torch.Tensor | None = None, x3: torch.Tensor | None = None,
+                       dy2: torch.Tensor | None = None, dy3: torch.Tensor | None = None,
+                       dres: torch.Tensor | None = None, eps: float = 1e-5,
+                       write_y: bool = True, group=None, exact_order: bool = True,
+                       fwd_bwd_fn: Callable | None = None,
+                       reduce_fn: Callable | None = None):
+    """The RMSNorm forward recomputed in its backward (ops.rmsnorm_fwd_bwd)
+    on this rank's rows, dweight summed over all ranks.
+
+    Returns (y or None, dx for the local rows, global fp32 dweight)."""
+    fwd_bwd_fn = fwd_bwd_fn or ops.rmsnorm_fwd_bwd
+    reduce_fn = reduce_fn or ops.dw_reduce
+    y, _, dx, dw = fwd_bwd_fn(x, weight, dy, x2=x2, x3=x3, dy2=dy2, dy3=dy3, dres=dres, eps=eps,
+                              write_y=write_y, dw_dtype=torch.float32)
+    return y, dx, _sum_over_ranks(dw, group, exact_order, reduce_fn)
+
+
 def embedding_fwd_vocab_parallel(ids: torch.Tensor, table_shard: torch.Tensor, vocab_lo: int,
                                  vocab_total: int, *, group=None,
                                  fwd_fn: Callable | None = None) -> torch.Tensor:

@@ -1,7 +1,8 @@
 """Multi-rank host logic of kernelproblems_b200.sharding on CPU ranks (gloo,
 world size 2), with the CUDA kernels replaced by oracle functions: row
 sharding, the dweight exchange (all-gather + fixed-order sum, and plain
-all-reduce), the vocab-parallel embedding forward (masked gather +
+all-reduce) of the RMSNorm backward and of the forward recomputed in it, the
+vocab-parallel embedding forward (masked gather +
 all-reduce) and backward (per-rank table-gradient shard), and host-side
 failure detection (a rank that raises before a collective, and a rank that
 stalls until the process group's timeout ends the other rank's collective)."""
@@ -98,6 +99,38 @@ def _body_rms(rank, exact_order=True):
     return rows.lo, rows.hi, dx, dw
 
 
+def _cpu_fwd_bwd(x, w, dy, x2=None, x3=None, dy2=None, dy3=None, dres=None, eps=1e-5,
+                 write_y=True, dw_dtype=torch.float32):
+    from oracle import fragments as F
+    add = torch.ops.aten.add.Tensor
+    h = x if x2 is None else add(x, x2)
+    h = h if x3 is None else add(h, x3)
+    g = dy if dy2 is None else add(dy, dy2)
+    g = g if dy3 is None else add(g, dy3)
+    y, rstd = F.rmsnorm_fwd(h, w, eps)
+    dx, _ = F.rmsnorm_bwd(g, h, rstd, w)
+    if dres is not None:
+        dx = add(dres, dx)
+    return (y if write_y else None), rstd, dx, F.rmsnorm_dw_f64(g, h, rstd).float()
+
+
+def _fwd_bwd_inputs(M=37, N=64):
+    from kernelproblems_b200 import configs as cf
+    return ([cf.randn((M, N), seed=20 + i) for i in range(2)], cf.rmsnorm_weight(N, seed=22),
+            [cf.randn((M, N), seed=23 + i) for i in range(2)], cf.randn((M, N), seed=25))
+
+
+def _body_fwd_bwd(rank):
+    from kernelproblems_b200 import sharding
+    (x, x2), w, (dy, dy2), dres = _fwd_bwd_inputs()
+    rows = sharding.local_rows(x.shape[0])
+    sl = slice(rows.lo, rows.hi)
+    y, dx, dw = sharding.rmsnorm_fwd_bwd_dp(
+        x[sl].contiguous(), w, dy[sl].contiguous(), x2=x2[sl].contiguous(), dy2=dy2[sl].contiguous(),
+        dres=dres[sl].contiguous(), fwd_bwd_fn=_cpu_fwd_bwd, reduce_fn=_ordered_sum)
+    return rows.lo, rows.hi, y, dx, dw
+
+
 def _body_rms_allreduce(rank):
     return _body_rms(rank, exact_order=False)
 
@@ -164,6 +197,23 @@ def test_rmsnorm_bwd_dp_two_ranks(body):
         assert torch.allclose(dw.double(), full_dw, rtol=1e-5, atol=1e-4)
         dws.append(dw)
     assert torch.equal(dws[0], dws[1]), "every rank holds the same dweight"
+
+
+def test_rmsnorm_fwd_bwd_dp_two_ranks():
+    from oracle import fragments as F
+    out = run_ranks(_body_fwd_bwd)
+    assert all(s == "ok" for s, _ in out.values()), out
+    (x, x2), w, (dy, dy2), dres = _fwd_bwd_inputs()
+    full_y, _, full_dx, _ = _cpu_fwd_bwd(x, w, dy, x2=x2, dy2=dy2, dres=dres)
+    add = torch.ops.aten.add.Tensor
+    h, g = add(x, x2), add(dy, dy2)
+    _, rstd = F.rmsnorm_fwd(h, w, 1e-5)
+    full_dw = F.rmsnorm_dw_f64(g, h, rstd)
+    for r in range(WORLD):
+        lo, hi, y, dx, dw = out[r][1]
+        assert torch.equal(y, full_y[lo:hi]) and torch.equal(dx, full_dx[lo:hi]), "local rows only"
+        assert torch.allclose(dw.double(), full_dw, rtol=1e-5, atol=1e-4)
+    assert torch.equal(out[0][1][4], out[1][1][4]), "every rank holds the same dweight"
 
 
 def test_vocab_parallel_embedding_two_ranks():
