@@ -314,10 +314,10 @@ FRAG_API int frag_copy_rows(const void* src, int64_t src_stride, void* dst, int6
  * copies in ONE launch, CTAs shared out in proportion to each segment's
  * bytes.  The unshard of a whole FSDP parameter group out of one all-gather
  * buffer: replaces the nine split_with_sizes -> clone chains of
- *   v8/7815074de963/problem.py:18-75 and v8/94985bdb7630/problem.py:18-77
+ *   v8/7815074de963/problem.py:23-103 and v8/94985bdb7630/problem.py:23-106
  * (splits [512, 2097152, 524288, 524288, 2097152, 512, 7340032 x3] of the
  * [8, 27264000] view), and the weight + table pair of
- *   v5/013a3088b488/problem.py:18-36 and v8/8e33a91b7364/problem.py:18-51.
+ *   v5/013a3088b488/problem.py:23-55 and v8/8e33a91b7364/problem.py:23-51.
  * Segments with rows == 0 or row_bytes == 0 are skipped; no destination may
  * overlap a source or another destination.  When every segment is 16-byte
  * aligned (pointers, strides, row_bytes) the group is one launch; otherwise

@@ -3,7 +3,7 @@
 // [8, -1], split_with_sizes, clone of the [8, 65667072] split into a
 // contiguous [128256, 4096] table) and the small weight gathers of the other
 // FSDP fragments; the grouped form copies every split of one parameter group
-// (v8/7815074de963/problem.py:18-75) in a single launch.
+// (v8/7815074de963/problem.py:23-103) in a single launch.
 //
 // dst row r <- src row r, `row_bytes` each, rows `src_stride` / `dst_stride`
 // bytes apart.  With 16-byte aligned rows the copy moves 16-byte units, each

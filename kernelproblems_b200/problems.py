@@ -100,7 +100,7 @@ def add_rms_unshard_8e33a91b7364(mm_223, add_62, wait_tensor_969):
 
 
 def add_rms_unshard_t_013a3088b488(mm_223, add_62, wait_tensor_969):
-    """v5/013a3088b488/problem.py:15-40: as v8/8e33a91b7364, with the table
+    """v5/013a3088b488/problem.py:16-55: as v8/8e33a91b7364, with the table
     returned transposed for the lm_head -> (y [M, N], table.t() [4096, 128256])."""
     y, table = _add_rms_table(mm_223, add_62, wait_tensor_969)
     return (y, table.t())
@@ -129,7 +129,7 @@ def _add_rms_layer(mm, res, flat):
 
 
 def add_rms_layer_unshard_94985bdb7630(mm_216, add_60, wait_tensor_966):
-    """v8/94985bdb7630/problem.py:14-79: h = add_60 + mm_216, y =
+    """v8/94985bdb7630/problem.py:16-106: h = add_60 + mm_216, y =
     _fused_rms_norm(h, split 0 as the weight, 1e-5), and splits 1-7 of the
     [8, 27264000] view unsharded -> (y x3 [8192, 4096], [4096, 4096],
     [1024, 4096], [1024, 4096], [4096, 4096], [4096], [14336, 4096] x2)."""
@@ -138,7 +138,7 @@ def add_rms_layer_unshard_94985bdb7630(mm_216, add_60, wait_tensor_966):
 
 
 def add_rms_layer_unshard_7815074de963(mm_209, add_58, wait_tensor_963):
-    """v8/7815074de963/problem.py:14-77: as v8/94985bdb7630, with split 7
+    """v8/7815074de963/problem.py:16-103: as v8/94985bdb7630, with split 7
     returned as the raw contiguous clone [8, 7340032]."""
     y, shaped, parts = _add_rms_layer(mm_209, add_58, wait_tensor_963)
     return (y, y, y, *shaped[1:7], parts[7])

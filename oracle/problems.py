@@ -87,7 +87,7 @@ def add_rms_unshard_8e33a91b7364(mm_223, add_62, wait_tensor_969):
 
 
 def add_rms_unshard_t_013a3088b488(mm_223, add_62, wait_tensor_969):
-    """v5/013a3088b488/problem.py:15-40: v8/8e33a91b7364's graph, returning
+    """v5/013a3088b488/problem.py:16-55: v8/8e33a91b7364's graph, returning
     t(table) [4096, 128256]."""
     y, table = add_rms_unshard_8e33a91b7364(mm_223, add_62, wait_tensor_969)
     return (y, aten.t.default(table))
@@ -105,7 +105,7 @@ _LAYER_VIEWS = [[4096, 4096], [1024, 4096], [1024, 4096], [4096, 4096], [4096], 
 
 
 def _add_rms_layer(mm, res, flat):
-    """v8/94985bdb7630/problem.py:14-77: add, split_with_sizes of the
+    """v8/94985bdb7630/problem.py:16-106: add, split_with_sizes of the
     [8, 27264000] view, _fused_rms_norm with the split-0 weight, and the
     clones of splits 1-7 (split 8 unused)."""
     h = aten.add.Tensor(res, aten._unsafe_view.default(mm, [1, 8192, 4096]))
@@ -118,13 +118,13 @@ def _add_rms_layer(mm, res, flat):
 
 
 def add_rms_layer_unshard_94985bdb7630(mm_216, add_60, wait_tensor_966):
-    """v8/94985bdb7630/problem.py:14-79 -> (y x3, splits 1-7 unsharded)."""
+    """v8/94985bdb7630/problem.py:16-106 -> (y x3, splits 1-7 unsharded)."""
     y, views, last = _add_rms_layer(mm_216, add_60, wait_tensor_966)
     return (y, y, y, *views, aten._unsafe_view.default(last, [14336, 4096]))
 
 
 def add_rms_layer_unshard_7815074de963(mm_209, add_58, wait_tensor_963):
-    """v8/7815074de963/problem.py:14-77 -> as 94985bdb7630 with split 7 the
+    """v8/7815074de963/problem.py:16-103 -> as 94985bdb7630 with split 7 the
     raw clone [8, 7340032]."""
     y, views, last = _add_rms_layer(mm_209, add_58, wait_tensor_963)
     return (y, y, y, *views, last)
