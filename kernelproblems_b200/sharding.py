@@ -8,7 +8,8 @@ own rows with no communication.  Two fragments have a real exchange step:
     per-rank vectors are all-gathered and added in rank order by the same
     fixed-order kernel used inside a rank, so every rank gets bitwise the same
     dweight regardless of NCCL's reduction algorithm; ``exact_order=False``
-    uses a plain NCCL all-reduce instead.
+    uses a plain NCCL all-reduce instead.  The forward recomputed inside the
+    backward (``rmsnorm_fwd_bwd_dp``) exchanges its dweight the same way.
   * Vocab-parallel embedding: rank r owns table rows [lo_r, hi_r).  Forward:
     every rank gathers its own rows for the (replicated) ids, writing zero rows
     for ids it does not own, then the outputs are all-reduced; exactly one rank
@@ -35,6 +36,7 @@ __all__ = [
     "local_rows",
     "rmsnorm_bwd_dp",
     "add_rmsnorm_bwd_dp",
+    "rmsnorm_fwd_bwd_dp",
     "embedding_fwd_vocab_parallel",
     "embedding_bwd_vocab_parallel",
     "vocab_shard",

@@ -1,0 +1,45 @@
+"""The multi-GPU wrappers on one GPU with no process group (world size 1):
+the real kernels run and the wrappers must return exactly what the plain ops
+return (row range = all rows, no exchange).  The exchange itself is covered by
+tests/test_sharding_gloo.py on CPU ranks."""
+import pytest
+import torch
+
+from kernelproblems_b200 import configs as cf
+from kernelproblems_b200 import ops, sharding
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def test_local_rows_single_rank():
+    r = sharding.local_rows(37)
+    assert (r.lo, r.hi) == (0, 37)
+    v = sharding.vocab_shard(128256)
+    assert (v.lo, v.hi) == (0, 128256)
+
+
+def test_rmsnorm_dp_wrappers_equal_the_ops():
+    M, N = 96, 4096
+    x, x2 = cf.randn((M, N), seed=1).to(DEV), cf.randn((M, N), seed=2).to(DEV)
+    dy, dy2 = cf.randn((M, N), seed=3).to(DEV), cf.randn((M, N), seed=4).to(DEV)
+    dres = cf.randn((M, N), seed=5).to(DEV)
+    w = cf.rmsnorm_weight(N, seed=6).to(DEV)
+    _, rstd = ops.rmsnorm_fwd(x, w, 1e-5)
+    dx, dw = sharding.rmsnorm_bwd_dp(dy, x, rstd, w, eps=1e-5, dres=dres)
+    ex, ew = ops.rmsnorm_bwd(dy, x, rstd, w, eps=1e-5, dres=dres)
+    assert torch.equal(dx, ex) and torch.equal(dw, ew)
+    y, dx, dw = sharding.rmsnorm_fwd_bwd_dp(x, w, dy, x2=x2, dy2=dy2, dres=dres)
+    ey, _, ex, ew = ops.rmsnorm_fwd_bwd(x, w, dy, x2=x2, dy2=dy2, dres=dres)
+    assert torch.equal(y, ey) and torch.equal(dx, ex) and torch.equal(dw, ew)
+
+
+def test_vocab_parallel_embedding_single_rank():
+    ec = cf.EmbeddingCfg("dp1", (2, 64), 1000, 256)
+    ids = cf.embedding_ids(ec).to(DEV)
+    table = cf.randn((1000, 256), std=0.02, seed=7).to(DEV)
+    out = sharding.embedding_fwd_vocab_parallel(ids, table, 0, 1000)
+    assert torch.equal(out, ops.embedding_fwd(ids, table))
+    g = cf.randn((2, 64, 256), seed=8).to(DEV)
+    G = sharding.embedding_bwd_vocab_parallel(g, ids, 0, 1000, 1000)
+    assert torch.equal(G, ops.embedding_bwd(g, ids, 1000))
