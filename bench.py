@@ -16,12 +16,25 @@ the 126 MB L2 without an explicit flush):
   C4B  its backward           dy, dh, h -> d_res, dweight (+ exchange at N>1)
 
 `value` = algorithmic bytes of the step on all ranks / max-over-ranks device
-time per step (CUDA events on the launching stream, per-fragment CUDA graphs).
-At N>1 every rank runs its own batch (weak scaling); the only collective in
-the step is the dweight exchange of C1B and C4B, which runs on its own
-stream beside the fragments that follow it (the per-fragment breakdown times
-it inline instead).  The vocab-parallel embedding
-(masked gather + NCCL all-reduce of the output) is `--workload emb_vp`.
+time per step (CUDA events on the launching stream, CUDA graphs).  At N>1
+every rank runs its own batch (weak scaling); the only collective in the
+step is the dweight exchange of C1B and C4B, which runs on its own stream
+beside the fragments that follow it (C4B's beside the next step's first
+fragments; the per-fragment breakdown times it inline instead).
+
+After the timed steps, with the suite's results, the line carries:
+  parity            each rank's dweight (C1B, C4B) against the float64 column
+                    sum over all ranks' rows, and bit for bit against the
+                    rank-order sum of separately gathered per-rank vectors;
+  strong_scaling    C0F, C1B, C4F, C4B with the configured rows split over
+                    the ranks (one global problem), kernel and exchange ms
+                    apart, efficiency against each rank's own 1-GPU time;
+  emb_vp            the vocab-parallel embedding (masked gather + NCCL
+                    all-reduce of the output, per-rank gradient shard), with
+                    gather / all-reduce / backward ms and bit-exact parity;
+  triton_reference  (1 GPU) the reference's own Triton drop-ins beside this
+                    library's drop-ins for the same problems, same inputs;
+  e2e, cpu_baseline as the contract describes.
 
 `--impl reference` times the reference's torch-eager CPU graph (restated in
 oracle/fragments.py) on a row sample of the same workload on the host cores.
@@ -67,12 +80,14 @@ NEXT = ["C2N", "C3S", "C2C", "C2U", "C2S", "C2L", "C1R", "C1U", "C3X"]
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="suite",
                     help="suite | next | emb_vp | one fragment of " + ",".join(SUITE + NEXT))
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the strong-scaling, vocab-parallel and Triton-reference legs")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0,
@@ -112,83 +127,131 @@ def profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """SM clock, power and clock-event (throttle) reasons sampled during the
+    timed region, read-only.  NVML is polled from a thread every `period_s`
+    (5 ms), so even a timed region of a few tens of milliseconds carries a
+    dozen samples; nvidia-smi at 100 ms is the fallback when NVML is not
+    importable."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index: int, enabled: bool = True):
-        self.proc = None
-        self.path = None
+    def __init__(self, device: torch.device, enabled: bool = True, period_s: float = 0.005):
+        import threading
+        self.rows, self.t0, self.t1 = [], None, None
+        self.source = None
+        self.proc = self.thread = None
+        self.stop_ev = threading.Event()
         if not enabled:
             return
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            try:
+                h = pynvml.nvmlDeviceGetHandleByUUID(
+                    "GPU-" + str(torch.cuda.get_device_properties(device).uuid))
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(device.index or 0)
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            smax = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def poll():
+                while not self.stop_ev.is_set():
+                    try:
+                        self.rows.append(dict(
+                            t=time.monotonic(), sm=float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                            smax=float(smax), power=pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                            reasons=int(get_reasons(h))))
+                    except Exception:
+                        pass
+                    self.stop_ev.wait(period_s)
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            self.source = f"NVML every {period_s * 1e3:.0f} ms"
+        except Exception:
+            self._start_smi(device.index or 0)
+        t_end = time.monotonic() + 5.0  # sampling runs before the timed region starts
+        while not self.rows and time.monotonic() < t_end and self.source is not None:
+            if self.proc is not None:
+                self._read_smi()
+            time.sleep(0.01)
+
+    def _start_smi(self, idx):
         try:
             fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-i", str(gpu_index), "-lms", "100"],
+                 "-i", str(idx), "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            self.source = "nvidia-smi every 100 ms"
         except Exception:
             self.proc = None
-            return
-        # sampling is running before the timed region starts (a short region
-        # would otherwise end before nvidia-smi's first sample)
-        self._wait_lines(1, 5.0)
 
-    def _lines(self) -> int:
-        try:
-            return len(Path(self.path).read_text().splitlines())
-        except OSError:
-            return 0
-
-    def _wait_lines(self, n: int, limit_s: float) -> None:
-        t_end = time.monotonic() + limit_s
-        while self._lines() < n and time.monotonic() < t_end and self.proc.poll() is None:
-            time.sleep(0.01)
-
-    def start(self):
-        """Mark the start of the timed region: stop() waits for a sample after it."""
-        self.n0 = self._lines() if self.proc is not None else 0
-
-    def stop(self):
-        if self.proc is None:
-            return None
-        self._wait_lines(getattr(self, "n0", 0) + 1, 1.0)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
+    def _read_smi(self):
         rows = []
         for line in Path(self.path).read_text().splitlines():
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
             try:
-                rows.append(dict(sm=float(f[1]), smax=float(f[2]), power=float(f[3]),
-                                 hw=f[5], hwt=f[6], swt=f[7], swp=f[8]))
+                bits = 0
+                for name, col in (("hw_slowdown", 5), ("hw_thermal_slowdown", 6),
+                                  ("sw_thermal_slowdown", 7), ("sw_power_cap", 8)):
+                    if f[col].lower().startswith("active"):
+                        bits |= self.BITS[name]
+                rows.append(dict(t=None, sm=float(f[1]), smax=float(f[2]), power=float(f[3]),
+                                 reasons=bits))
             except ValueError:
                 continue
-        os.unlink(self.path)
+        self.rows = rows
+
+    def start(self):
+        """Mark the start of the timed region."""
+        self.t0 = time.monotonic()
+        self.n0 = len(self.rows)
+
+    def stop(self):
+        if self.source is None:
+            return None
+        self.t1 = time.monotonic()
+        # one more sample after the region ends
+        t_end = self.t1 + 1.0
+        while len(self.rows) <= getattr(self, "n0", 0) and time.monotonic() < t_end:
+            if self.proc is not None:
+                self._read_smi()
+            time.sleep(0.005)
+        self.stop_ev.set()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self._read_smi()
+            os.unlink(self.path)
+        n0 = getattr(self, "n0", 0)
+        rows = [r for r in self.rows if r["t"] is None or self.t0 <= r["t"] <= self.t1] \
+            if self.thread is not None else self.rows[max(0, n0 - 1):]
+        if not rows:  # region shorter than one period: the samples around it
+            rows = self.rows[max(0, n0 - 1): n0 + 1]
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "source": self.source}
         pmax = max(r["power"] for r in rows)
         load = [r for r in rows if r["power"] >= 0.5 * pmax] or rows
-        reasons = set()
-        for r in rows:
-            if r["hw"].lower().startswith("active"):
-                reasons.add("hw_slowdown")
-            if r["hwt"].lower().startswith("active"):
-                reasons.add("hw_thermal_slowdown")
-            if r["swt"].lower().startswith("active"):
-                reasons.add("sw_thermal_slowdown")
-            if r["swp"].lower().startswith("active"):
-                reasons.add("sw_power_cap")
+        reasons = sorted({name for r in rows for name, bit in self.BITS.items() if r["reasons"] & bit})
         return {"sm_mhz": statistics.median(r["sm"] for r in load),
                 "sm_max_mhz": max(r["smax"] for r in rows),
-                "reasons": sorted(reasons), "samples": len(rows),
-                "power_w_max": pmax}
+                "sm_mhz_min": min(r["sm"] for r in rows),
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": pmax, "source": self.source}
 
 
 def count_kernel_nodes(graph) -> int:
@@ -284,7 +347,14 @@ class Step:
         overlap = not events and any(seg[-1].exchange is not None for _, seg in graphs)
         if overlap and self.comm is None:
             self.comm = torch.cuda.Stream()
-        for g, seg in graphs:
+        if not hasattr(self, "ex_done"):
+            self.ex_done = [None] * len(graphs)
+        for si, (g, seg) in enumerate(graphs):
+            if overlap and self.ex_done[si] is not None:
+                # the previous step's exchange of this segment reads the
+                # dweight this segment is about to rewrite: order after it
+                # (it finished long ago in practice: a whole step runs between)
+                main.wait_event(self.ex_done[si])
             if g is not None:
                 g.replay()
             else:
@@ -294,26 +364,34 @@ class Step:
                 if overlap:
                     # The exchange (dweight all-gather + fixed-order sum) runs
                     # on its own stream after this segment's kernels, beside
-                    # the following fragments, none of which reads its result;
-                    # the step waits for it at the end.
+                    # the fragments that follow -- for the last segment, beside
+                    # the next step's first fragments -- none of which reads
+                    # its result.
                     done = torch.cuda.Event()
                     done.record(main)
                     self.comm.wait_event(done)
                     with torch.cuda.stream(self.comm):
                         last.exchange()
+                    ev = torch.cuda.Event()
+                    ev.record(self.comm)
+                    self.ex_done[si] = ev
                 else:
                     last.exchange()
                 if events:
                     last.ev_end.record()
-        if overlap:
-            main.wait_stream(self.comm)
+
+    def join(self):
+        """Order the current stream after every exchange still in flight."""
+        if self.comm is not None:
+            torch.cuda.current_stream().wait_stream(self.comm)
 
     def run(self):
         """One step as timed: no timing events inside; NCCL exchanges overlap
-        the fragments that follow them."""
+        the fragments that follow them (call join() before reading results)."""
         self._run(self.plain, events=False)
 
     def run_instrumented(self):
+        self.join()
         self._run(self.timed, events=True)
 
     def release(self):
@@ -408,6 +486,10 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
         f.host = dict(g=g, x=x, r=r) if dh is None else dict(g=g, x=x, r=r, dh=dh)
         f.e2e = lambda h: _e2e_call(lambda xs: ops.rmsnorm_bwd(xs["g"], xs["x"], xs["r"], w,
                                                                dres=xs.get("dh")), h)
+        # for the dweight parity check: the terms, this rank's dweight, the
+        # exchanged (global) dweight
+        f.dw_check = dict(g=g, x=x, r=r, local=(lambda: dw) if split_stages else (lambda: holder["dw"]),
+                          glob=(lambda: dwg) if world > 1 else None)
         return f
 
     def mk_c2(which):
@@ -784,10 +866,19 @@ def suite_descriptions(names, other: dict | None = None) -> dict:
     return {n: desc.get(n, (other or {}).get(n, n)) for n in names}
 
 
-def config_dict(workload, world, l2_note, fragments: dict):
+L2_NOTE = ("inputs larger than L2: each fragment's inputs were last touched a whole suite step "
+           "(about 22 GB of traffic per GPU) earlier, L2 is 0.126 GB; no explicit flush in the "
+           "timed steps")
+
+
+DATA = "synthetic (seeded generators with the configs' shapes and distributions)"
+
+
+def config_dict(workload, world, fragments: dict):
+    """The same dict from both arms for the same workload and world size."""
     return {"workload": workload, "fragments": fragments,
             "parallelism": f"dp{world} (rows per rank fixed; dweight exchange for C1B/C4B)",
-            "l2": l2_note}
+            "l2": L2_NOTE}
 
 
 def reference_arm(args, rank, world):
@@ -812,8 +903,8 @@ def reference_arm(args, rank, world):
     line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": UNIT,
             "n_gpus": world, "steps": steps, "warmup": warm,
             "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-            "config": config_dict(args.workload, 1, "n/a (CPU)", suite_descriptions(names)),
+            "vs_baseline": None, "dtype": "bf16", "data": DATA,
+            "config": config_dict(args.workload, world, suite_descriptions(names)),
             "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": torch.get_num_threads(),
                              "kind": "port",
                              "sample": (f"torch-eager CPU restatement of the reference graphs "
@@ -822,6 +913,557 @@ def reference_arm(args, rank, world):
             "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ------------------------------------------------------ parity and extra legs
+
+def _f64_colsum(g, x, r, chunk=8192):
+    """float64 column sums of g * x * r over the rows, and of the squared
+    terms (for a tolerance floor on near-zero columns); torch on the GPU,
+    chunked by rows."""
+    N = x.shape[-1]
+    g2, x2, r2 = g.reshape(-1, N), x.reshape(-1, N), r.reshape(-1)
+    s = torch.zeros(N, dtype=torch.float64, device=x.device)
+    q = torch.zeros_like(s)
+    for i in range(0, g2.shape[0], chunk):
+        t = g2[i:i + chunk].double() * x2[i:i + chunk].double() * r2[i:i + chunk, None].double()
+        s += t.sum(0)
+        q += t.pow(2).sum(0)
+    return s, q
+
+
+def _all_ok(flag: bool, dev, world) -> bool:
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def dweight_parity(g, x, r, local, glob, world, dev):
+    """The dweight a rank ends with, checked two ways:
+    * against the float64 column sum over every rank's rows (rtol 1e-4, with
+      a floor of 1e-4 x the column's L2 norm for near-zero columns);
+    * bit for bit against the fixed rank-order sum of every rank's own
+      dweight, gathered separately and reduced on this rank, and equal on
+      every rank."""
+    from kernelproblems_b200 import ops
+    s64, q64 = _f64_colsum(g, x, r)
+    if world > 1:
+        dist.all_reduce(s64)
+        dist.all_reduce(q64)
+    got = (glob if glob is not None else local).double()
+    err = (got - s64).abs()
+    bound = 1e-4 * s64.abs() + 1e-4 * q64.sqrt()
+    ok64 = bool((err <= bound).all().item())
+    rel = float((err / s64.abs().clamp_min(1e-30)).median().item())
+    out = {"vs_float64_rtol_1e-4": _all_ok(ok64, dev, world), "median_rel_err": rel}
+    if world > 1:
+        parts = torch.empty(world, local.numel(), dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(parts.view(-1), local.contiguous())
+        ref = ops.dw_reduce(parts)
+        same = torch.equal(ref, glob)
+        globs = torch.empty(world, glob.numel(), dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(globs.view(-1), glob.contiguous())
+        agree = all(torch.equal(globs[0], globs[i]) for i in range(world))
+        out["bitwise_rank_order_sum"] = _all_ok(same, dev, world)
+        out["ranks_agree_bitwise"] = _all_ok(agree, dev, world)
+    return out
+
+
+class L2Flush:
+    """Writes a 256 MB buffer (twice the 126 MB L2) between timed reps."""
+
+    def __init__(self, dev):
+        self.buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def __call__(self):
+        self.buf.zero_()
+
+
+def _time_reps(fn_kernels, fn_after, reps, flush, world):
+    """Per rep: flush L2, then events around fn_kernels() and fn_after()
+    (None: nothing).  Returns (mean kernel ms, mean total ms), max over ranks."""
+    ka, kb, kc = [], [], []
+    for _ in range(reps):
+        flush()
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record()
+        fn_kernels()
+        b.record()
+        if fn_after is not None:
+            fn_after()
+        c.record()
+        ka.append(a)
+        kb.append(b)
+        kc.append(c)
+    torch.cuda.synchronize()
+    k = statistics.fmean(a.elapsed_time(b) for a, b in zip(ka, kb))
+    t = statistics.fmean(a.elapsed_time(c) for a, c in zip(ka, kc))
+    v = torch.tensor([k, t], dtype=torch.float64, device=torch.cuda.current_device())
+    if world > 1:
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    return v[0].item(), v[1].item()
+
+
+def _graph_of(fn):
+    """fn captured into a CUDA graph after one eager warm-up call."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def strong_scaling_leg(dev, world, rank, pg, reps=20):
+    """The row-sharded configurations (C0, C1, C4 fwd and bwd) with a fixed
+    total: rank r takes rows [r*M/W, (r+1)*M/W) of one global problem (the
+    same seeded tensors on every rank), C1B and C4B add the dweight exchange
+    (all-gather of the per-rank vectors, fixed rank-order sum).  Each rank
+    also times the whole configuration alone, the 1-GPU reference of the
+    efficiency.  Kernel and exchange times are reported separately; all
+    times are means over reps with an L2 flush before each, max over ranks."""
+    from kernelproblems_b200 import configs as cf
+    from kernelproblems_b200 import ops
+    flush = L2Flush(dev)
+    out = {}
+    for name, c in (("C0F", cf.C0), ("C1B", cf.C1), ("C4F", cf.C4), ("C4B", cf.C4)):
+        M, N = c.M, c.N
+        sh = cf.shard_rows(M, world, rank)
+        w = cf.rmsnorm_weight(N, device=dev, seed=90)
+        full = {k: cf.randn((M, N), device=dev, seed=91 + i)
+                for i, k in enumerate(("x", "g", "dh") if name in ("C1B", "C4B") else ("x", "res"))}
+        if name == "C4B":  # the backward's input is the forward's h and its rstd
+            full["x"], _, _ = ops.add_rmsnorm_fwd(full["dh"], full["x"], w, c.eps, save_rstd=False)
+        if name in ("C1B", "C4B"):
+            _, full["r"] = ops.rmsnorm_fwd(full["x"], w, c.eps)
+
+        def call(t, ws=None):
+            if name == "C0F":
+                return ops.rmsnorm_fwd(t["x"], w, c.eps)
+            if name == "C4F":
+                return ops.add_rmsnorm_fwd(t["res"], t["x"], w, c.eps)
+            return ops.rmsnorm_bwd(t["g"], t["x"], t["r"], w, eps=c.eps,
+                                   dres=t["dh"] if name == "C4B" else None, workspace=ws)
+        rec = {"rows_total": M, "rows_per_rank_max": cf.shard_rows(M, world, 0).n}
+        # the whole configuration on this GPU alone
+        ws_full = torch.empty(ops.rmsnorm_bwd_workspace_bytes(M, N), dtype=torch.uint8, device=dev) \
+            if name in ("C1B", "C4B") else None
+        g_full = _graph_of(lambda: call(full, ws_full))
+        rec["full_1gpu_ms"], _ = _time_reps(g_full.replay, None, reps, flush, world)
+        del g_full, ws_full
+        shard = {k: v[sh.lo:sh.hi].contiguous() for k, v in full.items()}
+        del full
+        torch.cuda.empty_cache()
+        ws = torch.empty(max(16, ops.rmsnorm_bwd_workspace_bytes(sh.n, N)), dtype=torch.uint8, device=dev) \
+            if name in ("C1B", "C4B") else None
+        holder = {}
+
+        def local():
+            holder["out"] = call(shard, ws)
+        g_sh = _graph_of(local)
+        exchange = None
+        if name in ("C1B", "C4B") and world > 1:
+            pbuf = torch.empty(world, N, dtype=torch.float32, device=dev)
+            dwg = torch.empty(N, dtype=torch.float32, device=dev)
+
+            def exchange():
+                dist.all_gather_into_tensor(pbuf.view(-1), holder["out"][1], group=pg)
+                ops.dw_reduce(pbuf, out=dwg)
+        k_ms, t_ms = _time_reps(g_sh.replay, exchange, reps, flush, world)
+        nbytes = {"C0F": cf.bytes_rmsnorm_fwd, "C1B": cf.bytes_rmsnorm_bwd,
+                  "C4F": cf.bytes_add_rmsnorm_fwd, "C4B": cf.bytes_add_rmsnorm_bwd}[name](M, N)
+        rec.update({"kernel_ms": round(k_ms, 4), "exchange_ms": round(t_ms - k_ms, 4),
+                    "ms": round(t_ms, 4), "full_1gpu_ms": round(rec["full_1gpu_ms"], 4),
+                    "tokens_per_s": round(M / (t_ms * 1e-3)),
+                    "GB/s_aggregate": round(nbytes / (t_ms * 1e-3) / 1e9, 1),
+                    "speedup_vs_1gpu": round(rec["full_1gpu_ms"] / t_ms, 3),
+                    "efficiency": round(rec["full_1gpu_ms"] / (world * t_ms), 3)})
+        if name in ("C1B", "C4B"):
+            torch.cuda.synchronize()
+            rec["parity"] = dweight_parity(shard["g"], shard["x"], shard["r"], holder["out"][1],
+                                           dwg if world > 1 else None, world, dev)
+        out[name] = rec
+        del g_sh, shard, ws, holder
+        torch.cuda.empty_cache()
+    tot_full = sum(v["full_1gpu_ms"] for v in out.values())
+    tot = sum(v["ms"] for v in out.values())
+    return {"fragments": out, "sum_ms": round(tot, 4), "sum_full_1gpu_ms": round(tot_full, 4),
+            "efficiency": round(tot_full / (world * tot), 3),
+            "method": ("one global problem per configuration (same seeds on every rank), rank r "
+                       "takes its contiguous rows; kernels replayed from a CUDA graph, exchange "
+                       "(NCCL all-gather + fixed-order sum) eager; L2 flushed before each of "
+                       f"{reps} reps; efficiency = full-config 1-GPU ms / (N x sharded ms)")}
+
+
+def emb_vp_leg(dev, world, rank, pg, steps=30):
+    """Vocab-parallel embedding at the C2 shapes: rank r holds table rows
+    [lo_r, hi_r) (the 8-way split of the reference's FSDP layout at N = 8);
+    forward = masked gather of the replicated ids + NCCL all-reduce of the
+    bf16 [32768, 4096] output, backward = this rank's fp32 table-gradient
+    shard.  Gather, all-reduce and backward are timed separately (events per
+    step; max over ranks).  Parity: the all-reduced output equals a full
+    gather from the whole table bit for bit (rank 0 rebuilds the whole table
+    from every shard's seed), and each rank's gradient shard equals the same
+    rows of the unsharded backward."""
+    from kernelproblems_b200 import configs as cf
+    from kernelproblems_b200 import ops, sharding
+    c = cf.C2
+    sh = cf.shard_rows(c.vocab, world, rank)
+    ids = cf.embedding_ids(c, device=dev)
+    table = cf.randn((sh.n, c.dim), std=0.02, device=dev, seed=7 + 1000 * sh.lo)
+    g = cf.randn((*c.batch, c.dim), device=dev, seed=8)
+    Gs = torch.empty(sh.n, c.dim, dtype=torch.float32, device=dev)
+    ws = torch.empty(max(16, ops._lib.load().frag_embedding_bwd_workspace_bytes(c.T, sh.n)),
+                     dtype=torch.uint8, device=dev)
+    out = torch.empty(*c.batch, c.dim, dtype=torch.bfloat16, device=dev)
+
+    def bwd():
+        sharding.embedding_bwd_vocab_parallel(
+            g, ids, sh.lo, sh.n, c.vocab,
+            bwd_fn=lambda *a, **k: ops.embedding_bwd(*a, **k, out=Gs, workspace=ws))
+    for _ in range(3):
+        ops.embedding_fwd(ids, table, vocab_lo=sh.lo, vocab_total=c.vocab, out=out)
+        if world > 1:
+            dist.all_reduce(out, group=pg)
+        bwd()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    evs = []
+    for _ in range(steps):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        e[0].record()
+        ops.embedding_fwd(ids, table, vocab_lo=sh.lo, vocab_total=c.vocab, out=out)
+        e[1].record()
+        if world > 1:
+            dist.all_reduce(out, group=pg)
+        e[2].record()
+        bwd()
+        e[3].record()
+        evs.append(e)
+    torch.cuda.synchronize()
+    gather = statistics.fmean(e[0].elapsed_time(e[1]) for e in evs)
+    ar = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
+    bw = statistics.fmean(e[2].elapsed_time(e[3]) for e in evs)
+    total = evs[0][0].elapsed_time(evs[-1][3]) / steps
+    v = torch.tensor([gather, ar, bw, total], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    gather, ar, bw, total = v.tolist()
+    # parity (outside the timed region)
+    parts = [cf.randn((cf.shard_rows(c.vocab, world, r).n, c.dim), std=0.02, device=dev,
+                      seed=7 + 1000 * cf.shard_rows(c.vocab, world, r).lo) for r in range(world)] \
+        if rank == 0 else None
+    fwd_ok = True
+    if rank == 0:
+        full = torch.cat(parts)
+        del parts
+        fwd_ok = torch.equal(out, ops.embedding_fwd(ids, full))
+        del full
+    Gfull = ops.embedding_bwd(g, ids, c.vocab)
+    bwd_ok = torch.equal(Gs, Gfull[sh.lo:sh.hi])
+    del Gfull
+    torch.cuda.empty_cache()
+    out_bytes = c.T * c.dim * cf.BF16
+    peer = _emb_vp_peer(dev, world, pg, ids, table, sh, c, out, gather + ar, steps)
+    nb = cf.bytes_embedding_fwd(c.T, c.dim) + cf.bytes_embedding_bwd(c.T, c.dim, c.vocab)
+    return {"ms_per_step": round(total, 4), "gather_ms": round(gather, 4),
+            "allreduce_ms": round(ar, 4), "bwd_shard_ms": round(bw, 4),
+            "allreduce_bytes": out_bytes,
+            "allreduce_busbw_GBs": (round(2 * (world - 1) / world * out_bytes / (ar * 1e-3) / 1e9, 1)
+                                    if world > 1 else None),
+            "GB/s_aggregate": round(nb / (total * 1e-3) / 1e9, 1),
+            "tokens_per_s": round(c.T / (total * 1e-3)), "steps": steps,
+            "parity": {"fwd_bit_exact_vs_full_gather": _all_ok(fwd_ok, dev, world),
+                       "bwd_shard_equals_unsharded_rows": _all_ok(bwd_ok, dev, world)},
+            "fused_peer_fwd": peer,
+            "layout": f"vocab{world}: rank r owns table rows [r*V/W, (r+1)*V/W), ids and grad replicated",
+            "scaling": "strong (fixed 32768 tokens, table split over ranks)"}
+
+
+def _emb_vp_peer(dev, world, pg, ids, table, sh, c, ref_out, nccl_fwd_ms, steps):
+    """The same vocab-parallel forward with the exchange fused into the gather
+    over NVLink peer memory (sharding.PeerVocabParallelEmbedding): forward ms
+    (events, mean, max over ranks) and bit-exact parity with the NCCL path's
+    output (itself checked against the full gather)."""
+    from kernelproblems_b200 import sharding
+    pe, err = None, ""
+    try:
+        pe = sharding.PeerVocabParallelEmbedding(c.T, c.dim, group=pg, device=dev)
+    except Exception as e:  # reported; every rank agrees below before using it
+        err = repr(e)[:200]
+    if not _all_ok(pe is not None, dev, world):
+        if pe is not None:
+            pe.close()
+        return {"error": err or "another rank could not set up its peer buffers"}
+    try:
+        for _ in range(3):
+            pe(ids, table, sh.lo, c.vocab)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        evs = []
+        for _ in range(steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            o = pe(ids, table, sh.lo, c.vocab)
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        ms = torch.tensor([statistics.fmean(a.elapsed_time(b) for a, b in evs)], dtype=torch.float64,
+                          device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = ms.item()
+        same = torch.equal(o.view_as(ref_out), ref_out)
+        from kernelproblems_b200 import _lib as L
+        flags = L.load().frag_device_errors(1)
+        out_bytes = c.T * c.dim * 2
+        return {"fwd_ms": round(ms, 4),
+                "nvlink_GBs_per_rank_out": (round((world - 1) / world * out_bytes / (ms * 1e-3) / 1e9, 1)
+                                            if world > 1 else None),
+                "speedup_vs_gather_plus_allreduce": round(nccl_fwd_ms / ms, 3),
+                "parity_bit_exact_vs_nccl_path": _all_ok(same and flags == 0, dev, world),
+                "steps": steps,
+                "design": ("owner gathers each row once and stores it into every rank's output over "
+                           "CUDA IPC peer mappings; bounded flag barriers (entry, exit); no multicast")}
+    finally:
+        pe.close()
+
+
+def _freqs_cis(dim, end, theta, dev):
+    """torchtitan's precompute_freqs_cis: complex64 [end, dim/2]."""
+    f = 1.0 / (theta ** (torch.arange(0, dim, 2, device=dev)[: dim // 2].float() / dim))
+    t = torch.arange(end, device=dev, dtype=torch.float32)
+    return torch.polar(torch.ones(end, dim // 2, device=dev), torch.outer(t, f))
+
+
+def problem_inputs(cfg, dev):
+    """Inputs of the reference problem(s) a configuration comes from, in the
+    problems' own formats (get_inputs() order) at the configuration's size,
+    seeded: {problem: [inputs]}, and the algorithmic bytes of one call under
+    the problems' own contracts."""
+    from kernelproblems_b200 import configs as cf
+    if cfg == "C0F":
+        c = cf.C0
+        return {"v8/f4e9e58fef73": [cf.randn(c.shape, device=dev, seed=1),
+                                    cf.rmsnorm_weight(c.N, device=dev, seed=2)]}, \
+            cf.bytes_rmsnorm_fwd(c.M, c.N)
+    if cfg == "C1B":
+        c = cf.C1
+        return {"v7/45990c83cfd6": [cf.randn(c.shape, device=dev, seed=3),
+                                    cf.rmsnorm_weight(c.N, device=dev, seed=4),
+                                    cf.randn(c.shape, device=dev, seed=5)]}, \
+            3 * c.M * c.N * 2 + 4 * c.N  # x, dy, dx; w, dw (bf16): rstd recomputed
+    if cfg in ("C2F", "C2B"):
+        c = cf.C2
+        ids = cf.embedding_ids(c, device=dev)
+        if cfg == "C2F":
+            return {"v7/1e49beb8a123": [cf.randn((c.vocab * c.dim,), std=0.02, device=dev, seed=6),
+                                        ids]}, cf.bytes_embedding_fwd(c.T, c.dim)
+        return {"v7/a12a160cb11b": [cf.randn((*c.batch, c.dim), device=dev, seed=7), ids]}, \
+            cf.bytes_embedding_bwd(c.T, c.dim, c.vocab)
+    if cfg in ("C3F", "C3B"):
+        c = cf.C3
+        T = c.T
+        pos = cf.rope_positions(c, device=dev).view(1, T)
+        if cfg == "C3F":
+            fr = _freqs_cis(c.D, c.S, c.theta, dev)
+            return {"v8/c8c60d8f7015": [pos.to(torch.int32), fr,
+                                        cf.randn((T, c.Hq * c.D), device=dev, seed=8),
+                                        cf.randn((T, c.Hk * c.D), device=dev, seed=9)]}, \
+                cf.bytes_rope(T, c.Hq, c.Hk, c.D) - T * 8 + T * 4 + fr.numel() * 8
+        conj = _freqs_cis(c.D, c.S, c.theta, dev)[pos.view(-1)].conj().resolve_conj() \
+            .view(1, T, 1, c.D // 2).contiguous()
+        gq = cf.randn((T * c.Hq * c.D,), device=dev, seed=10).as_strided(
+            [1, c.Hq, T, c.D], [T * c.Hq * c.D, c.D, c.Hq * c.D, 1])
+        gk = cf.randn((T * c.Hk * c.D,), device=dev, seed=11).as_strided(
+            [1, c.Hk, T, c.D], [T * c.Hk * c.D, c.D, c.Hk * c.D, 1])
+        return {"v7/bfe872e373e4": [gq, conj], "v7/5c65f62b0422": [gk, conj]}, \
+            4 * T * (c.Hq + c.Hk) * c.D + 2 * T * (c.D // 2) * 8
+    c = cf.C4
+    M, N = c.M, c.N
+    w = cf.rmsnorm_weight(N, device=dev, seed=12)
+    if cfg == "C4F":
+        return {"v8/7884328a5557": [cf.randn((M, N), device=dev, seed=13),
+                                    cf.randn((1, M, N), device=dev, seed=14), w]}, \
+            3 * M * N * 2 + 2 * N  # res, x read; y written (the problem returns y only)
+    h = cf.randn((1, M, N), device=dev, seed=15)
+    r = torch.rsqrt(h.float().pow(2).mean(-1, keepdim=True) + c.eps)
+    return {"v7/7f544ceb2120": [cf.randn((M, N), device=dev, seed=16),
+                                cf.randn((1, M, N), device=dev, seed=17), h, r, w,
+                                cf.randn((1, M, N), device=dev, seed=18)]}, \
+        5 * M * N * 2 + 4 * M + 2 * N + 4 * N
+
+
+def pcie_leg(dev, world, nbytes=1 << 30, reps=5):
+    """Host <-> device copy bandwidth of this rank alone and with every rank
+    copying at once: 1 GiB pinned buffers, H2D, D2H, and both directions at
+    the same time on two streams (GB/s per rank, min over ranks)."""
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    h2 = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    d2 = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    out = {}
+    for name in ("h2d", "d2h", "both"):
+        d.copy_(h, non_blocking=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            if name in ("h2d", "both"):
+                with torch.cuda.stream(s1):
+                    d.copy_(h, non_blocking=True)
+            if name in ("d2h", "both"):
+                with torch.cuda.stream(s2):
+                    h2.copy_(d2, non_blocking=True)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        gbs = torch.tensor([nbytes * reps * (2 if name == "both" else 1) / dt / 1e9], device=dev)
+        if world > 1:
+            dist.all_reduce(gbs, op=dist.ReduceOp.MIN)
+        out[name + "_GBs_per_rank"] = round(gbs.item(), 1)
+    out["note"] = ("1 GiB pinned copies, every rank at once (wall clock over 5 copies, min over ranks); "
+                   "PCIe Gen5 x16 is 64 GB/s per direction nominal")
+    return out
+
+
+def e2e_dropin(dev, world, reps=3):
+    """Each configuration's reference problem(s) through this library's
+    drop-in kernel_function (kernelproblems_b200.problems, the reference's own
+    calling contract): inputs uploaded from pinned host memory, the call,
+    every output copied back to pinned host memory, all inside the events
+    (mean of `reps` after a warm-up).  Configurations run one at a time; a
+    step is their sum."""
+    from kernelproblems_b200 import problems
+    per, tot_ms, tot_b, tot_in, tot_out = {}, 0.0, 0, 0, 0
+    for cfg in SUITE:
+        probs, nbytes = problem_inputs(cfg, dev)
+        host = {p: [t.cpu().pin_memory() for t in inp] for p, inp in probs.items()}
+        del probs
+        torch.cuda.empty_cache()
+        outs_h = {}
+
+        def one():
+            nin = nout = 0
+            for p, hin in host.items():
+                xs = [t.to(dev, non_blocking=True) for t in hin]
+                o = problems.get_kernel_function(p)(*xs)
+                o = o if isinstance(o, (tuple, list)) else (o,)
+                bufs = outs_h.setdefault(p, [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in o])
+                for b, t in zip(bufs, o):
+                    b.copy_(t, non_blocking=True)
+                nin += sum(t.numel() * t.element_size() for t in hin)
+                nout += sum(t.numel() * t.element_size() for t in o)
+            return nin, nout
+        one()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            nin, nout = one()
+        b.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([a.elapsed_time(b) / reps], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = ms.item()
+        per[cfg] = {"problems": list(host), "ms": round(ms, 3), "h2d_bytes": nin, "d2h_bytes": nout,
+                    "GB/s_algorithmic": round(nbytes / (ms * 1e-3) / 1e9, 1)}
+        tot_ms += ms
+        tot_b += nbytes
+        tot_in += nin
+        tot_out += nout
+        del host, outs_h
+        torch.cuda.empty_cache()
+    return {"value": round(world * tot_b / (tot_ms * 1e-3) / 1e9, 2), "unit": UNIT,
+            "ms_per_step": round(tot_ms, 3), "h2d_bytes_per_step": tot_in, "d2h_bytes_per_step": tot_out,
+            "fragments": per,
+            "path": ("kernelproblems_b200.problems.get_kernel_function(problem)(*inputs) with inputs "
+                     "from pinned host memory and outputs copied back, the problems' own contracts "
+                     "and algorithmic bytes (as in triton_reference)")}
+
+
+def triton_leg(dev, reps=10):
+    """The reference's Triton drop-ins (oracle/_ref/triton, fetched by
+    oracle/triton_ref.py) and this library's drop-ins for the same problems,
+    on the same inputs at each configuration's size, each call replayed from
+    a CUDA graph with an L2 flush before each rep (mean ms).  Parity: each
+    output of the reference kernel against ours (bf16 outputs atol 1e-2 /
+    rtol 1.6e-2, the embedding gather bit for bit, fp32 table gradient and
+    dweight rtol 1e-4 with a small floor)."""
+    from oracle import triton_ref
+    if not triton_ref.available():
+        return {"unavailable": "oracle/_ref/triton is missing (python oracle/triton_ref.py --reference <checkout>)"}
+    from kernelproblems_b200 import configs as cf
+    from kernelproblems_b200 import problems
+    flush = L2Flush(dev)
+    res = {}
+
+    def close(a, b, cfg, addend=None):
+        """a (reference kernel) against b (ours)."""
+        if cfg == "C2F":
+            return bool(torch.equal(a, b))
+        if a.dtype != b.dtype or a.shape != b.shape:
+            return False
+        af, bf = a.double(), b.double()
+        if a.dtype == torch.float32:  # rstd, fp32 dweight, fp32 table gradient
+            atol = 1e-5 if cfg == "C2B" else 1e-4 * bf.abs().mean().item()
+            return bool(((af - bf).abs() <= 1e-4 * bf.abs() + atol).all())
+        tol = 1e-2 + 1.6e-2 * bf.abs()
+        if addend is not None:
+            # bf16(dres + dx): the reference kernel adds the unrounded dx, the
+            # graph (and this library) bf16(dx); one ulp of |dx| may survive
+            # cancellation
+            t = (bf - addend.double()).abs().clamp_min(2.0 ** -126)
+            tol = tol + torch.exp2(torch.floor(torch.log2(t)) - 7)
+        return bool(((af - bf).abs() <= tol).all())
+
+    for cfg in ("C0F", "C1B", "C2F", "C2B", "C3F", "C3B", "C4F", "C4B"):
+        probs, nbytes = problem_inputs(cfg, dev)
+        rec = {"problems": list(probs), "bytes": nbytes}
+        ours_ms = ref_ms = 0.0
+        parity = True
+        for prob, inp in probs.items():
+            f_ours = problems.get_kernel_function(prob)
+            f_ref = triton_ref.kernel_function(prob)
+            o1 = f_ours(*inp)
+            o2 = f_ref(*inp)
+            torch.cuda.synchronize()
+            o1 = o1 if isinstance(o1, (tuple, list)) else (o1,)
+            o2 = o2 if isinstance(o2, (tuple, list)) else (o2,)
+            addend = inp[5] if cfg == "C4B" else None
+            parity = parity and len(o1) == len(o2) and all(
+                close(b, a, cfg, addend if a.dtype == torch.bfloat16 else None)
+                for a, b in zip(o1, o2))
+            del o1, o2
+            g1 = _graph_of(lambda: f_ours(*inp))
+            g2 = _graph_of(lambda: f_ref(*inp))
+            ours_ms += _time_reps(g1.replay, None, reps, flush, 1)[0]
+            ref_ms += _time_reps(g2.replay, None, reps, flush, 1)[0]
+            del g1, g2
+        rec.update({"ours_ms": round(ours_ms, 4), "triton_ms": round(ref_ms, 4),
+                    "ours_GB/s": round(nbytes / (ours_ms * 1e-3) / 1e9, 1),
+                    "triton_GB/s": round(nbytes / (ref_ms * 1e-3) / 1e9, 1),
+                    "speedup_vs_triton": round(ref_ms / ours_ms, 3),
+                    "parity_triton_vs_ours": parity})
+        res[cfg] = rec
+        del probs
+        torch.cuda.empty_cache()
+    return {"fragments": res,
+            "method": ("each problem's reference kernel_function (oracle/_ref/triton, size patches "
+                       "listed in oracle/triton_ref.py) and this library's drop-in for the same "
+                       "problem on the same inputs at the configuration's size; one call per CUDA "
+                       f"graph, L2 flushed before each of {reps} reps; the problems' own contracts "
+                       "(C1B recomputes rstd and returns a bf16 dweight, C3 is the interleaved "
+                       "complex layout with a freqs table, C4F returns y only, C4B sums two "
+                       "gradients)")}
 
 
 def ours_arm(args, rank, local_rank, world):
@@ -834,7 +1476,15 @@ def ours_arm(args, rank, local_rank, world):
         pg = dist.group.WORLD
     _lib.load()
     if args.workload == "emb_vp":
-        return emb_vp_arm(args, rank, world, dev, pg)
+        line = {"metric": METRIC, "unit": UNIT, "n_gpus": world, "emb_vp": emb_vp_leg(dev, world, rank, pg,
+                                                                                     args.steps)}
+        line["value"] = line["emb_vp"]["GB/s_aggregate"]
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return 0
     names = {"suite": SUITE, "next": NEXT}.get(args.workload, [args.workload])
     frags = build_suite(dev, world, rank, names, pg, args.rows_frac)
     step = Step(frags, not args.no_graphs)
@@ -843,11 +1493,12 @@ def ours_arm(args, rank, local_rank, world):
 
     for _ in range(max(3, args.warmup)):
         step.run()
+    step.join()
     torch.cuda.synchronize()
     K = args.steps
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(local_rank, enabled=(rank == 0 and not args.no_clocks))
+    clocks = ClockSampler(dev, enabled=(rank == 0 and not args.no_clocks))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -855,16 +1506,25 @@ def ours_arm(args, rank, local_rank, world):
     t_start.record(stream)
     for _ in range(K):
         step.run()
+    step.join()  # the last step's exchange is inside the timed region
     t_end.record(stream)
     torch.cuda.synchronize()
+    clk = clocks.stop()
     if world > 1:
         dist.barrier()
-    clk = clocks.stop()
     total_ms = t_start.elapsed_time(t_end)
+    # dweight parity of the timed step's results (every rank, same order)
+    parity = {}
+    for f in frags:
+        chk = getattr(f, "dw_check", None)
+        if chk is not None:
+            parity[f.name] = dweight_parity(chk["g"], chk["x"], chk["r"], chk["local"](),
+                                            chk["glob"]() if chk["glob"] else None, world, dev)
     # per-fragment / per-stage breakdown: the same step replayed R more times,
-    # read from the events inside the step after each replay
+    # read from the events inside the step after each replay (exchanges inline)
     R = max(5, min(K, 30))
     frag_ms = {f.name: [] for f in frags}
+    ex_ms = {f.name: [] for f in frags}
     stage_ms = {f.name: [[] for _ in f.stages] for f in frags}
     for _ in range(R):
         if world > 1:
@@ -872,12 +1532,16 @@ def ours_arm(args, rank, local_rank, world):
             torch.cuda.synchronize()  # exchange absorbs another rank's skew
         step.run_instrumented()
         torch.cuda.synchronize()
-        for name, (fm, st) in step.breakdown().items():
-            frag_ms[name].append(fm)
+        for f in frags:
+            st = [f.ev[i].elapsed_time(f.ev[i + 1]) for i in range(len(f.stages))]
+            frag_ms[f.name].append(f.ev[0].elapsed_time(f.ev[-1]))
+            if f.ev_end is not None:
+                ex_ms[f.name].append(f.ev[-1].elapsed_time(f.ev_end))
             for i, v in enumerate(st):
-                stage_ms[name][i].append(v)
+                stage_ms[f.name][i].append(v)
     # max over ranks
-    tmax = torch.tensor([total_ms] + [statistics.fmean(frag_ms[f.name]) for f in frags],
+    tmax = torch.tensor([total_ms] + [statistics.fmean(frag_ms[f.name]) for f in frags]
+                        + [statistics.fmean(ex_ms[f.name]) if ex_ms[f.name] else 0.0 for f in frags],
                         dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
@@ -886,6 +1550,7 @@ def ours_arm(args, rank, local_rank, world):
     value = world * step_bytes / (ms_step * 1e-3) / 1e9
     tokens = sum(f.tokens for f in frags)
     peak, peak_note = measured_peak()
+    nf = len(frags)
 
     fr = {}
     for i, f in enumerate(frags):
@@ -897,7 +1562,8 @@ def ours_arm(args, rank, local_rank, world):
                       "bytes": f.bytes, "tokens": f.tokens,
                       "stages_ms": {lab: round(statistics.fmean(stage_ms[f.name][si]), 4)
                                     for si, (lab, _) in enumerate(f.stages)}}
-    roof = None
+        if f.exchange is not None:
+            fr[f.name]["exchange_ms_inline"] = round(tmax[1 + nf + i], 4)
     dom = next((f for f in frags if f.name == DOMINANT), frags[0])
     main_ms = statistics.fmean(stage_ms[dom.name][0])
     achieved = dom.bytes / (main_ms * 1e-3) / 1e9
@@ -917,24 +1583,34 @@ def ours_arm(args, rank, local_rank, world):
     line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded generators with the configs' shapes and distributions)",
+            "data": DATA,
             "config": config_dict(args.workload, world,
-                                  "inputs larger than L2 across a step: each fragment's inputs were last "
-                                  f"touched one step ({step_bytes / 1e9:.2f} GB of traffic, L2 0.126 GB) "
-                                  "earlier; no explicit flush",
                                   suite_descriptions([f.name for f in frags],
                                                      {f.name: f.desc for f in frags})),
+            "timed_region_ms": round(total_ms, 2),
             "pct_of_8TBs_per_gpu": round(100 * value / world / NOMINAL_HBM_GBS, 1),
             "frac_of_measured_per_gpu": round(value / world / peak, 3),
             "tokens_per_s_sum_over_fragments": round(world * tokens / (ms_step * 1e-3)),
-            "fragments": fr, "roofline": roof, "clocks": clk, "gpu_launches": launches}
+            "fragments": fr, "roofline": roof, "clocks": clk, "gpu_launches": launches,
+            "parity": parity}
+    step.release()
+    if args.workload == "suite" and args.rows_frac == 1.0 and not args.no_extra:
+        # the row-sharded configurations at a fixed total (strong scaling), the
+        # vocab-parallel embedding, and (one GPU) the reference's Triton kernels
+        line["strong_scaling"] = strong_scaling_leg(dev, world, rank, pg)
+        line["emb_vp"] = emb_vp_leg(dev, world, rank, pg)
+        if world == 1:
+            line["triton_reference"] = triton_leg(dev)
 
     # e2e through the public API with host buffers (every step: H2D inputs, D2H outputs)
     if not args.no_e2e:
         line["e2e"] = e2e_measure(frags, args.e2e_steps, world, dev, step_bytes)
+        if args.workload == "suite" and args.rows_frac == 1.0 and not args.no_extra:
+            line["e2e"]["pcie"] = pcie_leg(dev, world)
+            if world == 1:  # the same per-rank path at every N; at N>1 it only adds host contention
+                line["e2e"]["dropin"] = e2e_dropin(dev, world)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and set(names) <= set(SUITE):
         line["cpu_baseline"] = cpu_baseline(names, args.cpu_seconds)
-    step.release()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -998,60 +1674,6 @@ def e2e_measure(frags, steps, world, dev, step_bytes):
             "path": "kernelproblems_b200.ops public API, inputs from pinned host memory, "
                     "every output copied back to pinned host memory; uploads and read-backs on "
                     "their own streams, overlapping neighbouring fragments' kernels"}
-
-
-def emb_vp_arm(args, rank, world, dev, pg):
-    """Vocab-parallel embedding over the group: the table is split into `world`
-    contiguous vocab shards; fwd = masked gather + NCCL all-reduce of the
-    [32768, 4096] bf16 output; bwd = each rank's fp32 table-gradient shard."""
-    from kernelproblems_b200 import configs as cf
-    from kernelproblems_b200 import ops, sharding
-    c = cf.C2
-    sh = cf.shard_rows(c.vocab, world, rank)
-    ids = cf.embedding_ids(c, device=dev)
-    table = cf.randn((sh.n, c.dim), std=0.02, device=dev, seed=7 + rank)
-    g = cf.randn((*c.batch, c.dim), device=dev, seed=8)
-    Gs = torch.empty(sh.n, c.dim, dtype=torch.float32, device=dev)
-    ws = torch.empty(max(16, ops._lib.load().frag_embedding_bwd_workspace_bytes(c.T, sh.n)),
-                     dtype=torch.uint8, device=dev)
-    out = torch.empty(*c.batch, c.dim, dtype=torch.bfloat16, device=dev)
-
-    def step():
-        ops.embedding_fwd(ids, table, vocab_lo=sh.lo, vocab_total=c.vocab, out=out)
-        if world > 1:
-            dist.all_reduce(out, group=pg)
-        sharding.embedding_bwd_vocab_parallel(
-            g, ids, sh.lo, sh.n, c.vocab,
-            bwd_fn=lambda *a, **k: ops.embedding_bwd(*a, **k, out=Gs, workspace=ws))
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(args.steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    t = torch.tensor([a.elapsed_time(b) / args.steps], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.barrier()
-        dist.destroy_process_group()
-    ms = t.item()
-    nb = cf.bytes_embedding_fwd(c.T, c.dim) + cf.bytes_embedding_bwd(c.T, c.dim, c.vocab)
-    if rank == 0:
-        print(json.dumps({"metric": METRIC, "value": round(nb / (ms * 1e-3) / 1e9, 1), "unit": UNIT,
-                          "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
-                          "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-                          "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-                          "tokens_per_s": round(c.T / (ms * 1e-3)),
-                          "config": {"workload": "emb_vp: vocab-parallel embedding fwd (masked gather + "
-                                                 "NCCL all-reduce) + bwd (fp32 shard gradient), C2 shapes",
-                                     "parallelism": f"vocab{world}"}}), flush=True)
-    return 0
 
 
 def main(argv=None):

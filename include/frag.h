@@ -174,6 +174,12 @@ FRAG_API int frag_rmsnorm_fwd_bwd(const void* x, const void* x2, const void* x3,
  * per-block dweight partials [G, N] (whether or not dw was requested), which
  * multi-GPU callers may reduce across ranks themselves. */
 FRAG_API int64_t frag_rmsnorm_bwd_num_blocks(int64_t M, int64_t N);
+/* G for a given alignment: a call whose row pointers (dy, dy2, dy3, x, w,
+ * dres, dx_out, and for frag_rmsnorm_fwd_bwd x2, x3, y_out) are not all
+ * 16-byte aligned takes the generic kernels, whose row blocks differ.  Pass
+ * aligned = 0 for such a call to learn the G its partials were written with.
+ * No reference counterpart (a query of this library's own plan). */
+FRAG_API int64_t frag_rmsnorm_bwd_plan_blocks(int64_t M, int64_t N, int aligned);
 /* Sum partials[G, N] over G in order into dw (fp32) and/or dw_bf16. */
 FRAG_API int frag_dw_reduce(const float* partials, int64_t G, int64_t N, float* dw,
                    void* dw_bf16, frag_stream_t stream);
@@ -188,11 +194,15 @@ FRAG_API int frag_dw_reduce(const float* partials, int64_t G, int64_t N, float* 
  * plugin host whose ABI hands over tensors but neither an allocator nor a
  * workspace argument.
  * Arguments and results are those of frag_rmsnorm_bwd without the workspace.
- * The scratch (per-block dweight partials; for the generic kernel also a copy
- * of rstd) lives in one static device array of FRAG_NOALLOC_SCRATCH_BYTES
+ * The scratch lives in one static device array of FRAG_NOALLOC_SCRATCH_BYTES
  * (16 MiB) that every GPU loading this library holds until the process exits.
- * A problem whose scratch would not fit returns FRAG_ERR_SCRATCH_LIMIT before
- * anything is launched (the C1 and C4 configurations need about 4.9 MB).
+ * It holds the per-block dweight partials (at most 296 x N floats, 9.7 MB at
+ * N = 8192, for 16-byte aligned rows with N % 8 == 0 and N <= 8192) and, only
+ * when the generic kernels run (other widths or unaligned rows), also a copy
+ * of rstd (M floats).  A problem whose scratch would not fit returns
+ * FRAG_ERR_SCRATCH_LIMIT before anything is launched; with the generic
+ * kernels that limits M to about 4 million rows (the C1 and C4
+ * configurations need about 4.9 MB).
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress, with that device current).  Make that first call
  *     before any stream capture.
@@ -222,6 +232,45 @@ FRAG_API int frag_embedding_fwd(const int64_t* ids, const void* table, void* out
                        int64_t T, int64_t shard_rows, int64_t D,
                        int64_t vocab_lo, int64_t vocab_total, int32_t* status,
                        frag_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Vocab-parallel embedding forward fused with its exchange over NVLink peer
+ * memory (one process per GPU, up to FRAG_PEER_MAX_RANKS ranks on one node).
+ * Replaces the masked gather + all-reduce of the [T, D] output for the
+ * 8-way vocab split of the reference's FSDP table layout
+ * (v7/1e49beb8a123/problem.py:16-23 gathered across ranks); no reference
+ * counterpart for the exchange itself (the reference is single-GPU).
+ *   rank r owns table rows [vocab_lo, vocab_lo + shard_rows); for each token
+ *   t whose id it owns it loads table_shard[id - vocab_lo] once and stores it
+ *   to out_ptrs[p] + t*D for every rank p (its own output included); ids
+ *   outside [0, vocab_total) give zero rows (written by rank 0) and set
+ *   FRAG_DEVFLAG_INDEX_OOB in *status.  On return (stream order) this rank's
+ *   output holds every token's row, bit exact.
+ * out_ptrs[p]: rank p's bf16 [T, D] output, mapped into this process
+ *   (frag_peer_open), out_ptrs[rank] this rank's own; flag_ptrs[p]: rank
+ *   p's block of 2 * world int32 flags, zero at creation; counter: this
+ *   rank's own int32, zero at creation.  All three come from frag_peer_alloc
+ *   buffers, exchanged once between the ranks as IPC handles.
+ * epoch: 1 on the first call, +1 on every later call, the same on every rank
+ *   (the barriers compare the flags against it).  Every rank calls with the
+ *   same T and the same epoch sequence; calls on one rank must be ordered on
+ *   one stream.  Every flag wait is bounded (~2 s): on expiry the wait sets
+ *   FRAG_DEVFLAG_WAIT_TIMEOUT in frag_device_errors() and returns.
+ * ------------------------------------------------------------------------- */
+#define FRAG_PEER_MAX_RANKS 8
+#define FRAG_IPC_HANDLE_BYTES 64
+/* cudaMalloc + zero fill of `bytes` of device memory whose IPC handle
+ * (FRAG_IPC_HANDLE_BYTES) another process opens with frag_peer_open. */
+FRAG_API int frag_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle);
+FRAG_API int frag_peer_open(const void* ipc_handle, void** dev_ptr);
+FRAG_API int frag_peer_close(void* dev_ptr);
+FRAG_API int frag_peer_free(void* dev_ptr);
+FRAG_API int frag_embedding_fwd_vp_peer(const int64_t* ids, const void* table_shard, int64_t T,
+                                        int64_t shard_rows, int64_t D, int64_t vocab_lo,
+                                        int64_t vocab_total, void* const* out_ptrs,
+                                        int32_t* const* flag_ptrs, int32_t* counter, int rank,
+                                        int world, int32_t epoch, int32_t* status,
+                                        frag_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Token-embedding gather fused with RMSNorm.

@@ -70,6 +70,8 @@ class RopeTensor(C.Structure):
 
 
 FRAG_COPY_MAX_SEGMENTS = 16
+FRAG_PEER_MAX_RANKS = 8
+FRAG_IPC_HANDLE_BYTES = 64
 
 
 class CopySegment(C.Structure):
@@ -105,8 +107,16 @@ SIGNATURES: dict[str, tuple] = {
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp,
                _sz, _vp]),
     "frag_rmsnorm_bwd_num_blocks": (_i64, [_i64, _i64]),
+    "frag_rmsnorm_bwd_plan_blocks": (_i64, [_i64, _i64, _int]),
     "frag_dw_reduce": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "frag_embedding_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "frag_peer_alloc": (_int, [_sz, C.POINTER(_vp), _vp]),
+    "frag_peer_open": (_int, [_vp, C.POINTER(_vp)]),
+    "frag_peer_close": (_int, [_vp]),
+    "frag_peer_free": (_int, [_vp]),
+    "frag_embedding_fwd_vp_peer": (
+        _int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, C.POINTER(_vp), C.POINTER(_vp), _vp, _int, _int,
+               C.c_int32, _vp, _vp]),
     "frag_embedding_rmsnorm_fwd": (
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
     "frag_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64]),

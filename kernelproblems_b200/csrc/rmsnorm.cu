@@ -802,9 +802,15 @@ BwdPlan make_bwd_plan(int64_t M, int64_t N, bool aligned) {
   return pl;
 }
 
+size_t bwd_partials_bytes(const BwdPlan& pl, int64_t N) {
+  return align_up(static_cast<size_t>(pl.G) * N * sizeof(float), 256);
+}
+size_t bwd_rstd_copy_bytes(int64_t M) { return align_up(static_cast<size_t>(M) * sizeof(float), 256); }
+
+// What a launch with this plan needs: the [G, N] partials, plus the rstd
+// copy (p.rws) that only the generic kernels keep.
 size_t bwd_workspace_bytes(const BwdPlan& pl, int64_t M, int64_t N) {
-  return align_up(static_cast<size_t>(pl.G) * N * sizeof(float), 256) +
-         align_up(static_cast<size_t>(M) * sizeof(float), 256);
+  return bwd_partials_bytes(pl, N) + (pl.tma ? 0 : bwd_rstd_copy_bytes(M));
 }
 
 template <bool HAS_DY2, bool HAS_DRES, bool RECOMPUTE, bool FWD = false>
@@ -831,6 +837,9 @@ int launch_bwd_t(const BwdPlan& pl, BwdIn p, int64_t M, int64_t N, float eps, cu
     rmsnorm_bwd_vec<2, HAS_DY2, HAS_DRES, RECOMPUTE><<<grid, T, 0, s>>>(p, M, static_cast<int>(N), eps, pl.rows_per_block);
     return check_launch();
   }
+  // the generic kernels keep a copy of rstd after the partials; a caller
+  // whose workspace was sized for the ring plan has no room for it
+  if (p.rws == nullptr) return FRAG_ERR_WORKSPACE;
   rmsnorm_bwd_generic_dx<HAS_DY2, HAS_DRES, RECOMPUTE, FWD>
       <<<dim3(static_cast<unsigned>(M)), 256, 0, s>>>(p, N, eps);
   int st = check_launch();
@@ -889,8 +898,10 @@ int rmsnorm_bwd_impl(bool fwd, const void* dy, const void* dy2, const void* dy3,
   p.dres = static_cast<const uint16_t*>(dres);
   p.dx = static_cast<uint16_t*>(dx_out);
   p.partials = static_cast<float*>(workspace);
-  p.rws = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                   align_up(static_cast<size_t>(pl.G) * N * sizeof(float), 256));
+  const size_t part_bytes = bwd_partials_bytes(pl, N);
+  p.rws = workspace_bytes >= part_bytes + bwd_rstd_copy_bytes(M)
+              ? reinterpret_cast<float*>(static_cast<char*>(workspace) + part_bytes)
+              : nullptr;
   p.x2 = static_cast<const uint16_t*>(x2);
   p.x3 = static_cast<const uint16_t*>(x3);
   p.y = static_cast<uint16_t*>(y_out);
@@ -935,16 +946,21 @@ int frag_add_rmsnorm_fwd(const void* res, const void* x, const void* w, void* h,
 
 size_t frag_rmsnorm_bwd_workspace_bytes(int64_t M, int64_t N) {
   if (M <= 0 || N <= 0) return 0;
-  // The generic plan (unaligned callers) never needs more than the vector one
-  // for the same M: both use at most sm_count * blocks_per_sm blocks.
+  // Enough for either plan (aligned or not) and for every kernel a plan may
+  // fall back to: the larger partials block plus the generic kernels' rstd copy.
   const BwdPlan a = make_bwd_plan(M, N, true);
   const BwdPlan b = make_bwd_plan(M, N, false);
-  return std::max(bwd_workspace_bytes(a, M, N), bwd_workspace_bytes(b, M, N));
+  return std::max(bwd_partials_bytes(a, N), bwd_partials_bytes(b, N)) + bwd_rstd_copy_bytes(M);
 }
 
 int64_t frag_rmsnorm_bwd_num_blocks(int64_t M, int64_t N) {
   if (M <= 0 || N <= 0) return 0;
   return make_bwd_plan(M, N, true).G;
+}
+
+int64_t frag_rmsnorm_bwd_plan_blocks(int64_t M, int64_t N, int aligned) {
+  if (M <= 0 || N <= 0) return 0;
+  return make_bwd_plan(M, N, aligned != 0).G;
 }
 
 int frag_dw_reduce(const float* partials, int64_t G, int64_t N, float* dw, void* dw_bf16,

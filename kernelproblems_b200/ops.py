@@ -78,6 +78,27 @@ def _need(t: torch.Tensor, name: str, dtype: torch.dtype, dev: torch.device | No
         raise ValueError(f"{name} is on {t.device}, expected {dev}")
 
 
+def _check_out(t: torch.Tensor, name: str, dtype: torch.dtype, dev: torch.device, *,
+               shape: tuple | None = None, numel: int | None = None) -> torch.Tensor:
+    """A caller-supplied output buffer is written by the kernel as one dense
+    block of `shape` (or `numel` elements), so it must be exactly that: the
+    right shape or element count, dtype and device, and contiguous.  Anything
+    else would let the kernel write past the buffer."""
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name}: shape {tuple(t.shape)} != {tuple(shape)}")
+    if numel is not None and t.numel() != numel:
+        raise ValueError(f"{name}: {t.numel()} elements, the kernel writes {numel}")
+    if t.dtype != dtype:
+        raise ValueError(f"{name}: dtype {t.dtype} != {dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if t.device != dev:
+        raise ValueError(f"{name} is on {t.device}, expected {dev}")
+    return t
+
+
 def _status_word(dev: torch.device) -> torch.Tensor:
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     w = _status_words.get(idx)
@@ -141,9 +162,12 @@ def rmsnorm_fwd(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, *,
     _need(weight, "weight", torch.bfloat16, x.device)
     N = weight.numel()
     M = _rows(x, N, "x")
-    y = torch.empty_like(x) if out is None else out
+    y = (torch.empty_like(x) if out is None
+         else _check_out(out, "out", torch.bfloat16, x.device, shape=x.shape))
     if save_rstd and rstd is None:
         rstd = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    elif save_rstd:
+        _check_out(rstd, "rstd", torch.float32, x.device, numel=M)
     wc = weight.contiguous()
     with _on_device(x.device):
         _lib.call("frag_rmsnorm_fwd", _ptr(x), _ptr(wc), _ptr(y),
@@ -163,8 +187,12 @@ def add_rmsnorm_fwd(residual: torch.Tensor, x: torch.Tensor, weight: torch.Tenso
     N = weight.numel()
     M = _rows(x, N, "x")
     _rows(residual, N, "residual")
-    h = (torch.empty_like(x) if h_out is None else h_out) if write_h else None
-    y = torch.empty_like(x) if y_out is None else y_out
+    h = None
+    if write_h:
+        h = (torch.empty_like(x) if h_out is None
+             else _check_out(h_out, "h_out", torch.bfloat16, x.device, shape=x.shape))
+    y = (torch.empty_like(x) if y_out is None
+         else _check_out(y_out, "y_out", torch.bfloat16, x.device, shape=x.shape))
     rstd = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device) if save_rstd else None
     wc = weight.contiguous()
     with _on_device(x.device):
@@ -292,7 +320,11 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,
         else:
             _lib.call("frag_rmsnorm_bwd3", _ptr(dy), _ptr(dy2), _ptr(dy3), *tail)
         if return_partials:
-            G = int(lib.frag_rmsnorm_bwd_num_blocks(M, N)) if M else 0
+            # the launch planned its row blocks from the alignment of every
+            # row pointer; ask for the plan of that same case
+            aligned = all(t.data_ptr() % 16 == 0
+                          for t in (dy, dy2, dy3, x, wc, dres, dx) if t is not None)
+            G = int(lib.frag_rmsnorm_bwd_plan_blocks(M, N, int(aligned))) if M else 0
             parts = workspace[: G * N * 4].view(torch.float32).view(G, N)
             return dx, dw, parts
     return dx, dw
@@ -307,6 +339,10 @@ def dw_reduce(partials: torch.Tensor, *, out: torch.Tensor | None = None,
     G, N = partials.shape
     if out is None and out_bf16 is None:
         out = torch.empty(N, dtype=torch.float32, device=partials.device)
+    if out is not None:
+        _check_out(out, "out", torch.float32, partials.device, numel=N)
+    if out_bf16 is not None:
+        _check_out(out_bf16, "out_bf16", torch.bfloat16, partials.device, numel=N)
     with _on_device(partials.device):
         _lib.call("frag_dw_reduce", _ptr(partials), G, N, _ptr(out), _ptr(out_bf16),
                   _stream(partials.device))
@@ -329,7 +365,8 @@ def embedding_fwd(ids: torch.Tensor, table: torch.Tensor, *, vocab_lo: int = 0,
     total = rows if vocab_total is None else int(vocab_total)
     ids_c = ids.contiguous()
     T = ids_c.numel()
-    o = torch.empty(*ids.shape, D, dtype=torch.bfloat16, device=ids.device) if out is None else out
+    o = (torch.empty(*ids.shape, D, dtype=torch.bfloat16, device=ids.device) if out is None
+         else _check_out(out, "out", torch.bfloat16, ids.device, shape=(*ids.shape, D)))
     with _on_device(ids.device):
         st = _status_word(ids.device)
         _lib.call("frag_embedding_fwd", _ptr(ids_c), _ptr(table), _ptr(o), T, rows, D,
@@ -384,7 +421,8 @@ def embedding_bwd(grad: torch.Tensor, ids: torch.Tensor, num_rows: int, *, vocab
         raise ValueError(f"grad {tuple(grad.shape)} does not match {T} ids x {D}")
     g = grad.contiguous()
     total = int(num_rows) if vocab_total is None else int(vocab_total)
-    G = torch.empty(num_rows, D, dtype=torch.float32, device=grad.device) if out is None else out
+    G = (torch.empty(num_rows, D, dtype=torch.float32, device=grad.device) if out is None
+         else _check_out(out, "out", torch.float32, grad.device, shape=(num_rows, D)))
     with _on_device(grad.device):
         lib = _lib.load()
         need = int(lib.frag_embedding_bwd_workspace_bytes(T, num_rows))
@@ -449,7 +487,8 @@ def rmsnorm_embedding_bwd(x: torch.Tensor, weight: torch.Tensor, ids: torch.Tens
         raise TypeError("dw_dtype must be float32 or bfloat16")
     ids_c = ids.contiguous()
     total = int(num_rows) if vocab_total is None else int(vocab_total)
-    G = torch.empty(num_rows, D, dtype=torch.float32, device=dev) if out is None else out
+    G = (torch.empty(num_rows, D, dtype=torch.float32, device=dev) if out is None
+         else _check_out(out, "out", torch.float32, dev, shape=(num_rows, D)))
     dw = torch.empty(D, dtype=dw_dtype, device=dev)
     y = torch.empty_like(x) if write_y else None
     d_emb = torch.empty_like(x) if return_d_emb else None

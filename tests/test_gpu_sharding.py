@@ -43,3 +43,26 @@ def test_vocab_parallel_embedding_single_rank():
     g = cf.randn((2, 64, 256), seed=8).to(DEV)
     G = sharding.embedding_bwd_vocab_parallel(g, ids, 0, 1000, 1000)
     assert torch.equal(G, ops.embedding_bwd(g, ids, 1000))
+
+
+def test_peer_vocab_parallel_embedding_single_rank():
+    """The fused peer-memory forward with one rank (no peers): its barriers
+    complete on its own flags and the output is the plain gather, bit for
+    bit, over repeated calls (the epoch advances)."""
+    ec = cf.EmbeddingCfg("peer1", (4, 100), 5000, 512)
+    ids = cf.embedding_ids(ec).to(DEV)
+    table = cf.randn((5000, 512), std=0.02, seed=9).to(DEV)
+    emb = sharding.PeerVocabParallelEmbedding(ids.numel(), 512)
+    try:
+        for _ in range(3):
+            out = emb(ids, table, 0, 5000)
+            assert torch.equal(out, ops.embedding_fwd(ids, table))
+        ops.check_status(torch.device(DEV))
+        bad = ids.clone()
+        bad[0, 0] = 5000  # outside the vocabulary: a zero row and the index flag
+        out = emb(bad, table, 0, 5000)
+        assert int(torch.count_nonzero(out[0, 0])) == 0
+        with pytest.raises(IndexError):
+            ops.check_status(torch.device(DEV))
+    finally:
+        emb.close()

@@ -8,6 +8,7 @@ failure detection (a rank that raises before a collective, and a rank that
 stalls until the process group's timeout ends the other rank's collective)."""
 import datetime
 import os
+import pickle
 import socket
 import traceback
 
@@ -33,7 +34,10 @@ def _entry(rank, fn, port, q, timeout_s):
         dist.init_process_group("gloo", rank=rank, world_size=WORLD,
                                 timeout=datetime.timedelta(seconds=timeout_s))
         res = fn(rank)
-        q.put((rank, "ok", res))
+        # plain pickle copies tensors by value: a torch queue would pass them
+        # through shared memory that this process may release before the
+        # parent has read it
+        q.put((rank, "ok", pickle.dumps(res)))
     except Exception as e:  # reported to the parent, which asserts on it
         q.put((rank, "error", f"{type(e).__name__}: {e}\n{traceback.format_exc()[-800:]}"))
     finally:
@@ -54,7 +58,7 @@ def run_ranks(fn, timeout_s=30):
     out = {}
     for _ in range(WORLD):
         r, status, res = q.get(timeout=timeout_s * 4)
-        out[r] = (status, res)
+        out[r] = (status, pickle.loads(res) if status == "ok" else res)
     for p in procs:
         p.join(timeout=timeout_s)
         if p.is_alive():

@@ -80,10 +80,24 @@ def test_no_alloc_matches_workspace_entry_point(shape, variant):
         assert_f32_close(dw, ref_dw, "dweight", atol=1e-4)
 
 
-def test_no_alloc_rejects_problems_beyond_its_scratch():
+@pytest.mark.parametrize("N", [1001, 4100])
+def test_no_alloc_rejects_problems_beyond_its_scratch(N):
     lib = _lib.load()
-    # generic kernel (N % 8 != 0) keeps a copy of rstd: 5M rows need 20 MB > 16 MiB
+    # widths with N % 8 != 0 run the generic kernels, which keep a copy of
+    # rstd next to the partials: 5M rows need 20 MB > 16 MiB.  Rejected
+    # before any launch, so the null pointers are never touched.
     st = lib.frag_rmsnorm_bwd_noalloc(None, None, None, None, None, None, None, None, None,
-                                      5_000_000, 1000, 1e-6, _stream())
+                                      5_000_000, N, 1e-6, _stream())
     assert st == 7
     assert b"static buffer" in lib.frag_status_string(st)
+
+
+def test_no_alloc_ring_plan_needs_no_rstd_copy():
+    """The ring kernel's scratch is only its [G, N] partials (G <= 2 per SM),
+    so many rows fit: the sizing counts the rstd copy only for the generic
+    kernels.  Checked through the plan query, without a launch."""
+    lib = _lib.load()
+    M, N = 5_000_000, 1000
+    G = lib.frag_rmsnorm_bwd_plan_blocks(M, N, 1)
+    assert 0 < G <= 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    assert G * N * 4 < (16 << 20) < G * N * 4 + M * 4
