@@ -53,7 +53,7 @@ emb_fwd_vec(const int64_t* __restrict__ ids, const uint16_t* __restrict__ table,
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const int c = c0 + u * 32 + lane;
-      buf[u] = (hit && c < chunks) ? ld_stream(src + c * 8) : make_uint4(0, 0, 0, 0);
+      buf[u] = (hit && c < chunks) ? ld_plain(src + c * 8) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {

@@ -11,8 +11,8 @@
 // rank instead of a ring all-reduce's 2(W-1)/W, there is no reduction
 // arithmetic, and the result is the table row bit for bit (no -0.0 -> +0.0).
 //
-// Two bounded flag barriers order the ranks (plain peer loads and stores, no
-// multicast):
+// Two bounded flag barriers order the ranks (plain peer loads and stores
+// only):
 //   entry  (one warp) every rank writes `epoch` into slot [0][rank] of every
 //          rank's flag block, then waits until all W slots [0][*] of its own
 //          block reach `epoch`.  A rank enters call k only after its stream
@@ -104,7 +104,7 @@ vp_gather_store(const __grid_constant__ PeerPtrs pp, const int64_t* __restrict__
 #pragma unroll
       for (int u = 0; u < UNROLL; ++u) {
         const int c = c0 + u * 32 + lane;
-        buf[u] = (mine && c < chunks) ? ld_stream(src + c * 8) : make_uint4(0, 0, 0, 0);
+        buf[u] = (mine && c < chunks) ? ld_plain(src + c * 8) : make_uint4(0, 0, 0, 0);
       }
       // the peers' copies first, this rank's own last: rank r starts with
       // peer r+1, so the W writers spread over the W destinations

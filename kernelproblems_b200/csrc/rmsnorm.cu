@@ -61,8 +61,8 @@ rmsnorm_fwd_vec(const uint16_t* __restrict__ x, const uint16_t* __restrict__ res
   for (int k = 0; k < VPT; ++k) {
     const int c = threadIdx.x + k * blockDim.x;
     if (c < chunks) {
-      xv[k] = ld_stream(x + base + c * 8);
-      if (HAS_RES) rv[k] = ld_stream(res + base + c * 8);
+      xv[k] = HAS_RES ? ld_plain(x + base + c * 8) : ld_stream(x + base + c * 8);
+      if (HAS_RES) rv[k] = ld_plain(res + base + c * 8);
       wv[k] = ld_cached(w + c * 8);
     } else {
       xv[k] = rv[k] = wv[k] = make_uint4(0, 0, 0, 0);
@@ -125,7 +125,7 @@ emb_rmsnorm_fwd_vec(const int64_t* __restrict__ ids, const uint16_t* __restrict_
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int c = threadIdx.x + k * blockDim.x;
-    xv[k] = (ok && c < chunks) ? ld_stream(src + c * 8) : make_uint4(0, 0, 0, 0);
+    xv[k] = (ok && c < chunks) ? ld_plain(src + c * 8) : make_uint4(0, 0, 0, 0);
     wv[k] = (c < chunks) ? ld_cached(w + c * 8) : make_uint4(0, 0, 0, 0);
   }
   float v[VPT][8];

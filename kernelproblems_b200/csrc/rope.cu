@@ -196,8 +196,8 @@ __global__ void __launch_bounds__(256) rope_vec(const RopeP p) {
       for (int u = 0; u < UNR; ++u) {
         const int h = h0 + u * HPI;
         if (h < T.H) {
-          va[u] = ld_stream(xb + h * T.xsh + oa);
-          vc[u] = ld_stream(xb + h * T.xsh + oc);
+          va[u] = ld_plain(xb + h * T.xsh + oa);
+          vc[u] = ld_plain(xb + h * T.xsh + oc);
         }
       }
 #pragma unroll

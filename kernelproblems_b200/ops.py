@@ -124,8 +124,12 @@ def check_status(device: torch.device | int | None = None) -> None:
         raise RuntimeError("a libfrag kernel's bounded wait expired; its outputs are invalid")
     if flags & _lib.FRAG_DEVFLAG_INDEX_OOB:
         raise IndexError("rope: a position was outside the freqs table")
-    devs = list(_status_words) if device is None else [torch.device("cuda", device).index
-                                                        if isinstance(device, int) else device.index]
+    if device is None:
+        devs = list(_status_words)
+    elif isinstance(device, int):
+        devs = [device]
+    else:  # torch.device("cuda") without an index means the current device
+        devs = [device.index if device.index is not None else cur]
     for idx in devs:
         w = _status_words.get(idx)
         if w is None:
@@ -268,7 +272,8 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,
                 dy3: torch.Tensor | None = None,
                 dres: torch.Tensor | None = None, eps: float = 1e-6,
                 dw_dtype: torch.dtype | None = torch.float32,
-                workspace: torch.Tensor | None = None, return_partials: bool = False):
+                workspace: torch.Tensor | None = None, return_partials: bool = False,
+                dx_out: torch.Tensor | None = None, dw_out: torch.Tensor | None = None):
     """RMSNorm backward.  Returns (dx, dw[, partials]).
 
     dy2   optional second gradient summed (in bf16) into dy first
@@ -276,6 +281,8 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,
     rstd  saved rstd (fp32, one per row) or None to recompute it with eps
     dres  optional residual gradient added (in bf16) to dx
     dw    fp32 (dw_dtype=torch.float32), bf16, or None (not reduced)
+    dx_out, dw_out  optional preallocated outputs (x-shaped bf16, N elements
+          of dw_dtype), written in place and returned
     partials  the [G, N] fp32 per-row-block sums, for cross-rank reductions
     """
     _need(dy, "dy", torch.bfloat16)
@@ -299,12 +306,14 @@ def rmsnorm_bwd(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,
         _need(rstd, "rstd", torch.float32, dev)
         if rstd.numel() != M or not rstd.is_contiguous():
             raise ValueError(f"rstd must be contiguous with {M} elements")
-    dx = torch.empty_like(x)
+    dx = (torch.empty_like(x) if dx_out is None
+          else _check_out(dx_out, "dx_out", torch.bfloat16, dev, shape=x.shape))
     dw = None
     if dw_dtype is not None:
         if dw_dtype not in (torch.float32, torch.bfloat16):
             raise TypeError("dw_dtype must be float32, bfloat16 or None")
-        dw = torch.empty(N, dtype=dw_dtype, device=dev)
+        dw = (torch.empty(N, dtype=dw_dtype, device=dev) if dw_out is None
+              else _check_out(dw_out, "dw_out", dw_dtype, dev, numel=N))
     with _on_device(dev):
         lib = _lib.load()
         need = int(lib.frag_rmsnorm_bwd_workspace_bytes(M, N))
