@@ -1023,7 +1023,7 @@ def strong_scaling_leg(dev, world, rank, pg, reps=20):
     efficiency.  Kernel and exchange times are reported separately; all
     times are means over reps with an L2 flush before each, max over ranks."""
     from kernelproblems_b200 import configs as cf
-    from kernelproblems_b200 import ops
+    from kernelproblems_b200 import ops, sharding
     flush = L2Flush(dev)
     out = {}
     for name, c in (("C0F", cf.C0), ("C1B", cf.C1), ("C4F", cf.C4), ("C4B", cf.C4)):
@@ -1061,15 +1061,35 @@ def strong_scaling_leg(dev, world, rank, pg, reps=20):
         def local():
             holder["out"] = call(shard, ws)
         g_sh = _graph_of(local)
-        exchange = None
+        exchange = peer = None
         if name in ("C1B", "C4B") and world > 1:
             pbuf = torch.empty(world, N, dtype=torch.float32, device=dev)
             dwg = torch.empty(N, dtype=torch.float32, device=dev)
+            dwp = torch.empty(N, dtype=torch.float32, device=dev)
 
             def exchange():
                 dist.all_gather_into_tensor(pbuf.view(-1), holder["out"][1], group=pg)
                 ops.dw_reduce(pbuf, out=dwg)
+            err = ""
+            try:  # the same exchange over NVLink peer memory, one launch
+                peer = sharding.PeerDweightExchange(N, group=pg, device=dev)
+            except Exception as e:  # every rank agrees below before using it
+                err = repr(e)[:200]
+            if not _all_ok(peer is not None, dev, world):
+                if peer is not None:
+                    peer.close()
+                peer = None
+                rec["exchange_peer_error"] = err or "another rank could not set up its peer buffers"
         k_ms, t_ms = _time_reps(g_sh.replay, exchange, reps, flush, world)
+        if peer is not None:
+            kp_ms, tp_ms = _time_reps(g_sh.replay, lambda: peer(holder["out"][1], out=dwp), reps, flush,
+                                      world)
+            torch.cuda.synchronize()
+            rec["exchange_peer_ms"] = round(tp_ms - kp_ms, 4)
+            rec["ms_peer"] = round(tp_ms, 4)
+            rec["efficiency_peer"] = round(rec["full_1gpu_ms"] / (world * tp_ms), 3)
+            rec["peer_equals_nccl_path_bitwise"] = _all_ok(torch.equal(dwp, dwg), dev, world)
+            peer.close()
         nbytes = {"C0F": cf.bytes_rmsnorm_fwd, "C1B": cf.bytes_rmsnorm_bwd,
                   "C4F": cf.bytes_add_rmsnorm_fwd, "C4B": cf.bytes_add_rmsnorm_bwd}[name](M, N)
         rec.update({"kernel_ms": round(k_ms, 4), "exchange_ms": round(t_ms - k_ms, 4),
@@ -1087,11 +1107,14 @@ def strong_scaling_leg(dev, world, rank, pg, reps=20):
         torch.cuda.empty_cache()
     tot_full = sum(v["full_1gpu_ms"] for v in out.values())
     tot = sum(v["ms"] for v in out.values())
+    tot_peer = sum(v.get("ms_peer", v["ms"]) for v in out.values())
     return {"fragments": out, "sum_ms": round(tot, 4), "sum_full_1gpu_ms": round(tot_full, 4),
             "efficiency": round(tot_full / (world * tot), 3),
+            "efficiency_peer_exchange": round(tot_full / (world * tot_peer), 3),
             "method": ("one global problem per configuration (same seeds on every rank), rank r "
                        "takes its contiguous rows; kernels replayed from a CUDA graph, exchange "
-                       "(NCCL all-gather + fixed-order sum) eager; L2 flushed before each of "
+                       "(NCCL all-gather + fixed-order sum; and, as *_peer, the NVLink peer-memory "
+                       "exchange) eager; L2 flushed before each of "
                        f"{reps} reps; efficiency = full-config 1-GPU ms / (N x sharded ms)")}
 
 

@@ -24,7 +24,9 @@
  *     FRAG_DEVFLAG_* bits; the call itself still returns FRAG_OK because the
  *     host cannot see device data without synchronising.
  *   - Entry points that need scratch memory take a caller-provided workspace
- *     and expose a *_workspace_bytes() size query; nothing here allocates.
+ *     and expose a *_workspace_bytes() size query; nothing here allocates
+ *     except frag_peer_alloc (the one-time buffers a multi-GPU peer exchange
+ *     shares between processes).
  */
 #ifndef FRAG_H_
 #define FRAG_H_
@@ -265,6 +267,20 @@ FRAG_API int frag_peer_alloc(size_t bytes, void** dev_ptr, void* ipc_handle);
 FRAG_API int frag_peer_open(const void* ipc_handle, void** dev_ptr);
 FRAG_API int frag_peer_close(void* dev_ptr);
 FRAG_API int frag_peer_free(void* dev_ptr);
+/* The dweight exchange of a data-parallel RMSNorm backward over NVLink peer
+ * memory (no reference counterpart: the reference is single-GPU; it replaces
+ * the all-gather + fixed-order sum of the [W, N] per-rank vectors).
+ *   dw_out[n] = sum over r = 0..world-1 of dw_local_r[n], added in rank order
+ *   (bitwise the same on every rank and equal to frag_dw_reduce of the
+ *   gathered [world, N] block).
+ * slot_ptrs[p]: rank p's fp32 [world, N] buffer, flag_ptrs[p]: rank p's
+ *   2 * world int32 flags, both from frag_peer_alloc (zero at creation) and
+ *   mapped with frag_peer_open; epoch as for frag_embedding_fwd_vp_peer.
+ *   One CTA per call; every wait bounded (~2 s, FRAG_DEVFLAG_WAIT_TIMEOUT,
+ *   dw_out not written).  N % 4 == 0, dw_local 16-byte aligned. */
+FRAG_API int frag_dw_exchange_peer(const float* dw_local, int64_t N, float* const* slot_ptrs,
+                                   int32_t* const* flag_ptrs, int rank, int world, int32_t epoch,
+                                   float* dw_out, frag_stream_t stream);
 FRAG_API int frag_embedding_fwd_vp_peer(const int64_t* ids, const void* table_shard, int64_t T,
                                         int64_t shard_rows, int64_t D, int64_t vocab_lo,
                                         int64_t vocab_total, void* const* out_ptrs,

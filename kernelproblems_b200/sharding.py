@@ -22,6 +22,10 @@ own rows with no communication.  Two fragments have a real exchange step:
 into the gather: each token's owner stores its row straight into every
 rank's output over NVLink peer memory (CUDA IPC), with bounded flag barriers
 instead of an all-reduce (frag_embedding_fwd_vp_peer).
+``PeerDweightExchange`` does the dweight exchange the same way: one
+single-CTA launch stores this rank's vector into every rank's slot row and
+sums the rows in rank order (frag_dw_exchange_peer), bitwise equal to the
+all-gather + fixed-order sum.
 
 The kernels default to ``kernelproblems_b200.ops``; the ``*_fn`` arguments
 exist so the host logic can be exercised on CPU ranks (gloo) in tests.
@@ -47,6 +51,7 @@ __all__ = [
     "embedding_bwd_vocab_parallel",
     "vocab_shard",
     "PeerVocabParallelEmbedding",
+    "PeerDweightExchange",
 ]
 
 
@@ -68,10 +73,12 @@ def vocab_shard(vocab: int, group=None) -> Rows:
 
 
 def _sum_over_ranks(dw: torch.Tensor, group, exact_order: bool,
-                    reduce_fn: Callable[[torch.Tensor], torch.Tensor]) -> torch.Tensor:
+                    reduce_fn: Callable[[torch.Tensor], torch.Tensor], peer=None) -> torch.Tensor:
     world, _ = _world(group)
     if world == 1:
         return dw
+    if peer is not None:
+        return peer(dw)
     if not exact_order:
         dist.all_reduce(dw, op=dist.ReduceOp.SUM, group=group)
         return dw
@@ -85,14 +92,17 @@ def rmsnorm_bwd_dp(dy: torch.Tensor, x: torch.Tensor, rstd: torch.Tensor | None,
                    exact_order: bool = True, dy2: torch.Tensor | None = None,
                    dres: torch.Tensor | None = None,
                    bwd_fn: Callable | None = None,
-                   reduce_fn: Callable | None = None):
+                   reduce_fn: Callable | None = None,
+                   peer: "PeerDweightExchange | None" = None):
     """RMSNorm backward on this rank's rows; dweight summed over all ranks.
 
+    peer: a PeerDweightExchange of the weight's size to exchange over NVLink
+    peer memory instead of NCCL (same result bit for bit as exact_order).
     Returns (dx for the local rows, global fp32 dweight)."""
     bwd_fn = bwd_fn or ops.rmsnorm_bwd
     reduce_fn = reduce_fn or ops.dw_reduce
     dx, dw = bwd_fn(dy, x, rstd, weight, dy2=dy2, dres=dres, eps=eps, dw_dtype=torch.float32)
-    return dx, _sum_over_ranks(dw, group, exact_order, reduce_fn)
+    return dx, _sum_over_ranks(dw, group, exact_order, reduce_fn, peer)
 
 
 def add_rmsnorm_bwd_dp(dy: torch.Tensor, dh: torch.Tensor, h: torch.Tensor,
@@ -153,6 +163,59 @@ class _DeviceArray:
                                          "version": 3, "strides": None}
 
 
+class _PeerBuffers:
+    """Device buffers shared between the ranks' processes over CUDA IPC: each
+    rank allocates one buffer per requested size (frag_peer_alloc, zero
+    filled), the ranks exchange the IPC handles once (all_gather_object on
+    the group) and map every peer's buffers (frag_peer_open).
+    ``ptrs[i][p]`` is rank p's buffer i as seen from this process."""
+
+    def __init__(self, sizes: list[int], group, device: torch.device):
+        world, rank = _world(group)
+        if world > _lib.FRAG_PEER_MAX_RANKS:
+            raise ValueError(f"at most {_lib.FRAG_PEER_MAX_RANKS} ranks")
+        self.world, self.rank, self.device = world, rank, device
+        self._own, self._opened = [], []
+        _lib.load()
+        with torch.cuda.device(device):
+            mine = [self._alloc(max(16, int(n))) for n in sizes]
+            handles = [None] * world
+            if world > 1:
+                dist.all_gather_object(handles, [h for _, h in mine], group=group)
+            else:
+                handles[0] = [h for _, h in mine]
+            self.ptrs = [[mine[i][0] if p == rank else self._open(handles[p][i]) for p in range(world)]
+                         for i in range(len(sizes))]
+
+    def _alloc(self, nbytes: int):
+        p = C.c_void_p()
+        h = (C.c_char * _lib.FRAG_IPC_HANDLE_BYTES)()
+        _lib.call("frag_peer_alloc", nbytes, C.byref(p), h)
+        self._own.append(p.value)
+        return p.value, bytes(h)
+
+    def _open(self, handle: bytes) -> int:
+        p = C.c_void_p()
+        h = (C.c_char * _lib.FRAG_IPC_HANDLE_BYTES).from_buffer_copy(handle)
+        _lib.call("frag_peer_open", h, C.byref(p))
+        self._opened.append(p.value)
+        return p.value
+
+    def array(self, i: int, offset: int = 0):
+        """ctypes array of every rank's buffer i (+ offset bytes)."""
+        return (C.c_void_p * self.world)(*[q + offset for q in self.ptrs[i]])
+
+    def close(self) -> None:
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            for p in self._opened:
+                lib.frag_peer_close(C.c_void_p(p))
+            for p in self._own:
+                lib.frag_peer_free(C.c_void_p(p))
+        self._own, self._opened = [], []
+
+
 class PeerVocabParallelEmbedding:
     """Vocab-parallel embedding forward with the exchange fused into the
     gather over NVLink peer memory.
@@ -173,52 +236,19 @@ class PeerVocabParallelEmbedding:
     """
 
     def __init__(self, max_tokens: int, dim: int, *, group=None, device: torch.device | None = None):
-        world, rank = _world(group)
-        if world > _lib.FRAG_PEER_MAX_RANKS:
-            raise ValueError(f"at most {_lib.FRAG_PEER_MAX_RANKS} ranks")
         if dim % 8 != 0:
             raise ValueError("dim must be a multiple of 8")
-        self.world, self.rank, self.group = world, rank, group
         self.max_tokens, self.dim = int(max_tokens), int(dim)
         self.device = device or torch.device("cuda", torch.cuda.current_device())
+        # output rows; flags [2][world] int32 at 0 and this rank's counter at 128
+        self._bufs = _PeerBuffers([self.max_tokens * self.dim * 2, 256], group, self.device)
+        self.world, self.rank = self._bufs.world, self._bufs.rank
         self.epoch = 0
-        self._own, self._opened = [], []
-        lib = _lib.load()
-        with torch.cuda.device(self.device):
-            out_ptr, out_h = self._alloc(lib, max(16, self.max_tokens * self.dim * 2))
-            ctl_ptr, ctl_h = self._alloc(lib, 256)  # flags [2][world] int32 at 0, counter at 128
-            handles = [None] * world
-            if world > 1:
-                dist.all_gather_object(handles, (out_h, ctl_h), group=group)
-            else:
-                handles[0] = (out_h, ctl_h)
-            outs, ctls = [], []
-            for p, (oh, ch) in enumerate(handles):
-                if p == rank:
-                    outs.append(out_ptr)
-                    ctls.append(ctl_ptr)
-                else:
-                    outs.append(self._open(lib, oh))
-                    ctls.append(self._open(lib, ch))
-        self._out_arr = (C.c_void_p * world)(*outs)
-        self._flag_arr = (C.c_void_p * world)(*ctls)
-        self._counter = C.c_void_p(ctl_ptr + 128)
-        self._buf = torch.as_tensor(_DeviceArray(out_ptr, (self.max_tokens, self.dim), "<i2"),
-                                    device=self.device).view(torch.bfloat16)
-
-    def _alloc(self, lib, nbytes: int):
-        p = C.c_void_p()
-        h = (C.c_char * _lib.FRAG_IPC_HANDLE_BYTES)()
-        _lib.call("frag_peer_alloc", nbytes, C.byref(p), h)
-        self._own.append(p.value)
-        return p.value, bytes(h)
-
-    def _open(self, lib, handle: bytes):
-        p = C.c_void_p()
-        h = (C.c_char * _lib.FRAG_IPC_HANDLE_BYTES).from_buffer_copy(handle)
-        _lib.call("frag_peer_open", h, C.byref(p))
-        self._opened.append(p.value)
-        return p.value
+        self._out_arr = self._bufs.array(0)
+        self._flag_arr = self._bufs.array(1)
+        self._counter = C.c_void_p(self._bufs.ptrs[1][self.rank] + 128)
+        self._buf = torch.as_tensor(_DeviceArray(self._bufs.ptrs[0][self.rank], (self.max_tokens, self.dim),
+                                                 "<i2"), device=self.device).view(torch.bfloat16)
 
     def __call__(self, ids: torch.Tensor, table_shard: torch.Tensor, vocab_lo: int,
                  vocab_total: int) -> torch.Tensor:
@@ -247,12 +277,47 @@ class PeerVocabParallelEmbedding:
         """Unmap the peers' buffers and free this rank's (after a sync)."""
         if self._buf is None:
             return
-        lib = _lib.load()
+        self._buf = None
+        self._bufs.close()
+
+
+class PeerDweightExchange:
+    """The dweight exchange of a row-sharded RMSNorm backward over NVLink
+    peer memory (frag_dw_exchange_peer): every rank passes its fp32 dweight
+    over its own rows and gets the sum over all ranks, added in rank order
+    (bitwise the same on every rank, and equal to ``ops.dw_reduce`` of the
+    all-gathered [world, N] block).  One single-CTA launch per call on the
+    current stream, in place of an NCCL all-gather (launch-latency bound at
+    16-32 KB) followed by the reduce.  All ranks call it equally often, in
+    the same order, on one stream each; ``close()`` frees the buffers."""
+
+    def __init__(self, n: int, *, group=None, device: torch.device | None = None):
+        if n % 4 != 0:
+            raise ValueError("n must be a multiple of 4")
+        self.n = int(n)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        world, _ = _world(group)
+        self._bufs = _PeerBuffers([world * self.n * 4, 256], group, self.device)
+        self.world, self.rank = self._bufs.world, self._bufs.rank
+        self.epoch = 0
+        self._slots = self._bufs.array(0)
+        self._flags = self._bufs.array(1)
+
+    def __call__(self, dw_local: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        if self._bufs is None:
+            raise RuntimeError("closed")
+        ops._need(dw_local, "dw_local", torch.float32, self.device)
+        if dw_local.numel() != self.n or not dw_local.is_contiguous():
+            raise ValueError(f"dw_local must be a contiguous fp32 tensor of {self.n} elements")
+        out = (torch.empty(self.n, dtype=torch.float32, device=self.device) if out is None
+               else ops._check_out(out, "out", torch.float32, self.device, numel=self.n))
+        self.epoch += 1
         with torch.cuda.device(self.device):
-            torch.cuda.synchronize()
-            self._buf = None
-            for p in self._opened:
-                lib.frag_peer_close(C.c_void_p(p))
-            for p in self._own:
-                lib.frag_peer_free(C.c_void_p(p))
-        self._own, self._opened = [], []
+            _lib.call("frag_dw_exchange_peer", ops._ptr(dw_local), self.n, self._slots, self._flags,
+                      self.rank, self.world, self.epoch, ops._ptr(out), ops._stream(self.device))
+        return out
+
+    def close(self) -> None:
+        if self._bufs is not None:
+            self._bufs.close()
+            self._bufs = None

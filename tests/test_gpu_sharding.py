@@ -66,3 +66,24 @@ def test_peer_vocab_parallel_embedding_single_rank():
             ops.check_status(torch.device(DEV))
     finally:
         emb.close()
+
+
+def test_peer_dweight_exchange_single_rank():
+    """One rank: the exchange returns its own vector (plus +0), bit for bit,
+    over repeated calls, and the wrapper passes it through rmsnorm_bwd_dp."""
+    N = 4096
+    ex = sharding.PeerDweightExchange(N)
+    try:
+        for seed in range(3):
+            v = torch.randn(N, generator=torch.Generator().manual_seed(seed)).to(DEV)
+            out = ex(v)
+            assert torch.equal(out, ops.dw_reduce(v.view(1, N)))
+        x, dy = cf.randn((64, N), seed=1).to(DEV), cf.randn((64, N), seed=2).to(DEV)
+        w = cf.rmsnorm_weight(N, seed=3).to(DEV)
+        _, rstd = ops.rmsnorm_fwd(x, w)
+        dx, dw = sharding.rmsnorm_bwd_dp(dy, x, rstd, w, peer=ex)
+        ex_dx, ex_dw = ops.rmsnorm_bwd(dy, x, rstd, w)
+        assert torch.equal(dx, ex_dx) and torch.equal(dw, ex_dw)
+        ops.check_status(torch.device(DEV))
+    finally:
+        ex.close()
