@@ -250,14 +250,15 @@ FRAG_API int frag_embedding_fwd(const int64_t* ids, const void* table, void* out
  *   output holds every token's row, bit exact.
  * out_ptrs[p]: rank p's bf16 [T, D] output, mapped into this process
  *   (frag_peer_open), out_ptrs[rank] this rank's own; flag_ptrs[p]: rank
- *   p's block of 2 * world int32 flags, zero at creation; counter: this
- *   rank's own int32, zero at creation.  All three come from frag_peer_alloc
- *   buffers, exchanged once between the ranks as IPC handles.
- * epoch: 1 on the first call, +1 on every later call, the same on every rank
- *   (the barriers compare the flags against it).  Every rank calls with the
- *   same T and the same epoch sequence; calls on one rank must be ordered on
- *   one stream.  Every flag wait is bounded (~2 s): on expiry the wait sets
- *   FRAG_DEVFLAG_WAIT_TIMEOUT in frag_device_errors() and returns.
+ *   p's block of 2 * world int32 flags, zero at creation; state: this rank's
+ *   own int32[2] (CTA counter, call count), zero at creation.  All three come
+ *   from frag_peer_alloc buffers, exchanged once between the ranks as IPC
+ *   handles.  Every rank calls with the same T, equally often; calls on one
+ *   rank must be ordered on one stream.  The call count advances on the
+ *   device, so the two launches take no per-call arguments and can be
+ *   captured in a CUDA graph.  Every flag wait is bounded (~2 s): on expiry
+ *   the wait sets FRAG_DEVFLAG_WAIT_TIMEOUT in frag_device_errors() and
+ *   returns.
  * ------------------------------------------------------------------------- */
 #define FRAG_PEER_MAX_RANKS 8
 #define FRAG_IPC_HANDLE_BYTES 64
@@ -275,18 +276,19 @@ FRAG_API int frag_peer_free(void* dev_ptr);
  *   gathered [world, N] block).
  * slot_ptrs[p]: rank p's fp32 [world, N] buffer, flag_ptrs[p]: rank p's
  *   2 * world int32 flags, both from frag_peer_alloc (zero at creation) and
- *   mapped with frag_peer_open; epoch as for frag_embedding_fwd_vp_peer.
- *   One CTA per call; every wait bounded (~2 s, FRAG_DEVFLAG_WAIT_TIMEOUT,
- *   dw_out not written).  N % 4 == 0, dw_local 16-byte aligned. */
+ *   mapped with frag_peer_open; state: this rank's own int32 call counter
+ *   (zero at creation, advanced by every call on the device).
+ *   One CTA per call, no per-call arguments (the launch can be captured in a
+ *   CUDA graph); every wait bounded (~2 s, FRAG_DEVFLAG_WAIT_TIMEOUT, dw_out
+ *   not written).  N % 4 == 0, dw_local 16-byte aligned. */
 FRAG_API int frag_dw_exchange_peer(const float* dw_local, int64_t N, float* const* slot_ptrs,
-                                   int32_t* const* flag_ptrs, int rank, int world, int32_t epoch,
+                                   int32_t* const* flag_ptrs, int32_t* state, int rank, int world,
                                    float* dw_out, frag_stream_t stream);
 FRAG_API int frag_embedding_fwd_vp_peer(const int64_t* ids, const void* table_shard, int64_t T,
                                         int64_t shard_rows, int64_t D, int64_t vocab_lo,
                                         int64_t vocab_total, void* const* out_ptrs,
-                                        int32_t* const* flag_ptrs, int32_t* counter, int rank,
-                                        int world, int32_t epoch, int32_t* status,
-                                        frag_stream_t stream);
+                                        int32_t* const* flag_ptrs, int32_t* state, int rank,
+                                        int world, int32_t* status, frag_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Token-embedding gather fused with RMSNorm.

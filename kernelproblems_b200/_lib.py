@@ -115,10 +115,10 @@ SIGNATURES: dict[str, tuple] = {
     "frag_peer_close": (_int, [_vp]),
     "frag_peer_free": (_int, [_vp]),
     "frag_dw_exchange_peer": (
-        _int, [_vp, _i64, C.POINTER(_vp), C.POINTER(_vp), _int, _int, C.c_int32, _vp, _vp]),
+        _int, [_vp, _i64, C.POINTER(_vp), C.POINTER(_vp), _vp, _int, _int, _vp, _vp]),
     "frag_embedding_fwd_vp_peer": (
         _int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, C.POINTER(_vp), C.POINTER(_vp), _vp, _int, _int,
-               C.c_int32, _vp, _vp]),
+               _vp, _vp]),
     "frag_embedding_rmsnorm_fwd": (
         _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp]),
     "frag_embedding_bwd_workspace_bytes": (_sz, [_i64, _i64]),

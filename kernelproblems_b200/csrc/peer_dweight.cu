@@ -18,7 +18,9 @@
 // rank gets the same bits, and they equal a fixed-order dw_reduce of the
 // gathered [W, N] block.  Every wait is bounded (~2 s): on expiry the kernel
 // sets FRAG_DEVFLAG_WAIT_TIMEOUT in the library's error word and returns
-// without writing dw_out.
+// without writing dw_out.  The call count (the epoch the flags are compared
+// against) lives in this rank's device state word and advances in the kernel,
+// so the launch has no per-call arguments and can be captured in a graph.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -63,8 +65,13 @@ __device__ bool flag_barrier(const PeerSlots& ps, int slot, int rank, int W, int
 
 __global__ void __launch_bounds__(1024)
 dw_exchange_peer(const float* __restrict__ dw_local, int N, const __grid_constant__ PeerSlots ps,
-                 int rank, int W, int32_t epoch, float* __restrict__ dw_out, int* err) {
-  __shared__ int s_ok;
+                 int rank, int W, int32_t* state, float* __restrict__ dw_out, int* err) {
+  __shared__ int s_ok, s_epoch;
+  if (threadIdx.x == 0) s_epoch = *state + 1;
+  __syncthreads();
+  const int32_t epoch = s_epoch;
+  // every rank advances its count identically, also when a wait gives up
+  if (threadIdx.x == 0) *state = epoch;
   if (threadIdx.x < 32) {
     const bool ok = flag_barrier(ps, 0, rank, W, epoch, err);
     if (threadIdx.x == 0) s_ok = ok;
@@ -104,9 +111,9 @@ dw_exchange_peer(const float* __restrict__ dw_local, int N, const __grid_constan
 using namespace frag;
 
 extern "C" int frag_dw_exchange_peer(const float* dw_local, int64_t N, float* const* slot_ptrs,
-                                     int32_t* const* flag_ptrs, int rank, int world, int32_t epoch,
+                                     int32_t* const* flag_ptrs, int32_t* state, int rank, int world,
                                      float* dw_out, frag_stream_t stream) {
-  if (world < 1 || world > FRAG_PEER_MAX_RANKS || rank < 0 || rank >= world || epoch < 1)
+  if (world < 1 || world > FRAG_PEER_MAX_RANKS || rank < 0 || rank >= world || !state)
     return FRAG_ERR_INVALID_ARG;
   if (N < 0 || !slot_ptrs || !flag_ptrs || (N > 0 && (!dw_local || !dw_out))) return FRAG_ERR_INVALID_ARG;
   if (N % 4 != 0 || N > (1 << 24)) return FRAG_ERR_SHAPE;
@@ -119,6 +126,6 @@ extern "C" int frag_dw_exchange_peer(const float* dw_local, int64_t N, float* co
   }
   if (N > 0 && !aligned16(dw_local)) return FRAG_ERR_ALIGN;
   dw_exchange_peer<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      dw_local, static_cast<int>(N), ps, rank, world, epoch, dw_out, device_error_word());
+      dw_local, static_cast<int>(N), ps, rank, world, state, dw_out, device_error_word());
   return check_launch();
 }

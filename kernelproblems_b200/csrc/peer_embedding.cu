@@ -24,7 +24,11 @@
 //          and waits for all W slots [1][*] of its own block: when the kernel
 //          ends, every peer's rows for this call are in this rank's buffer.
 // Every wait gives up after ~2 s of clock cycles, sets
-// FRAG_DEVFLAG_WAIT_TIMEOUT in the library's error word and returns.
+// FRAG_DEVFLAG_WAIT_TIMEOUT in the library's error word and returns.  The
+// call count (the epoch the flags are compared against) and the CTA counter
+// live in this rank's device state words; the exit barrier's last CTA
+// advances the count, so the launches take no per-call arguments and can be
+// captured in a graph.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -68,8 +72,10 @@ __device__ bool wait_all_ranks(const int32_t* own_flags, int slot, int W, int32_
   return __all_sync(0xffffffffu, ok);
 }
 
-__global__ void vp_entry_barrier(const __grid_constant__ PeerPtrs pp, int rank, int W, int32_t epoch,
+// state[0]: CTA counter of the exit barrier; state[1]: calls completed.
+__global__ void vp_entry_barrier(const __grid_constant__ PeerPtrs pp, int rank, int W, const int32_t* state,
                                  int* err) {
+  const int32_t epoch = state[1] + 1;
   const int lane = threadIdx.x & 31;
   if (lane < W) st_release_sys(pp.flags[lane] + 0 * W + rank, epoch);
   wait_all_ranks(pp.flags[rank], 0, W, epoch, err);
@@ -83,9 +89,11 @@ template <int UNROLL>
 __global__ void __launch_bounds__(256)
 vp_gather_store(const __grid_constant__ PeerPtrs pp, const int64_t* __restrict__ ids,
                 const uint16_t* __restrict__ table, int64_t T, int64_t shard_rows, int D,
-                int64_t vocab_lo, int64_t vocab_total, int rank, int W, int32_t epoch,
-                int32_t* counter, int32_t* status, int* err) {
+                int64_t vocab_lo, int64_t vocab_total, int rank, int W, int32_t* state,
+                int32_t* status, int* err) {
   __shared__ int s_last;
+  int32_t* counter = state;
+  const int32_t epoch = *reinterpret_cast<volatile int32_t*>(state + 1) + 1;
   const int lane = threadIdx.x & 31;
   const int chunks = D >> 3;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -131,6 +139,7 @@ vp_gather_store(const __grid_constant__ PeerPtrs pp, const int64_t* __restrict__
   __threadfence_system();
   if (lane < W) st_release_sys(pp.flags[lane] + 1 * W + rank, epoch);
   wait_all_ranks(pp.flags[rank], 1, W, epoch, err);
+  if (lane == 0) state[1] = epoch;  // this call is complete on this rank
 }
 
 }  // namespace
@@ -174,13 +183,11 @@ int frag_peer_free(void* dev_ptr) {
 
 int frag_embedding_fwd_vp_peer(const int64_t* ids, const void* table_shard, int64_t T,
                                int64_t shard_rows, int64_t D, int64_t vocab_lo, int64_t vocab_total,
-                               void* const* out_ptrs, int32_t* const* flag_ptrs, int32_t* counter,
-                               int rank, int world, int32_t epoch, int32_t* status,
-                               frag_stream_t stream) {
+                               void* const* out_ptrs, int32_t* const* flag_ptrs, int32_t* state,
+                               int rank, int world, int32_t* status, frag_stream_t stream) {
   if (world < 1 || world > FRAG_PEER_MAX_RANKS || rank < 0 || rank >= world) return FRAG_ERR_INVALID_ARG;
-  if (T < 0 || shard_rows < 0 || D < 0 || vocab_lo < 0 || vocab_total < 0 || epoch < 1)
-    return FRAG_ERR_INVALID_ARG;
-  if (!out_ptrs || !flag_ptrs || !counter || (T > 0 && !ids) || (shard_rows > 0 && !table_shard))
+  if (T < 0 || shard_rows < 0 || D < 0 || vocab_lo < 0 || vocab_total < 0) return FRAG_ERR_INVALID_ARG;
+  if (!out_ptrs || !flag_ptrs || !state || (T > 0 && !ids) || (shard_rows > 0 && !table_shard))
     return FRAG_ERR_INVALID_ARG;
   if (D % 8 != 0 || D > (1 << 20) || T > 0x7fffffffLL) return FRAG_ERR_SHAPE;
   PeerPtrs pp = {};
@@ -193,17 +200,18 @@ int frag_embedding_fwd_vp_peer(const int64_t* ids, const void* table_shard, int6
   if (shard_rows > 0 && !aligned16(table_shard)) return FRAG_ERR_ALIGN;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int* err = device_error_word();
-  vp_entry_barrier<<<1, 32, 0, s>>>(pp, rank, world, epoch, err);
+  vp_entry_barrier<<<1, 32, 0, s>>>(pp, rank, world, state, err);
   int st = check_launch();
   if (st != FRAG_OK) return st;
-  if (T == 0) return FRAG_OK;
   int sms = sm_count();
   if (sms <= 0) sms = 148;
   const int64_t need = ceil_div(T, 8);  // 8 warps (tokens) per CTA
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(need, static_cast<int64_t>(sms) * 8));
+  // at least one CTA even for T == 0: the exit barrier advances the count
+  const unsigned grid = static_cast<unsigned>(
+      std::max<int64_t>(1, std::min<int64_t>(need, static_cast<int64_t>(sms) * 8)));
   vp_gather_store<16><<<grid, 256, 0, s>>>(pp, ids, static_cast<const uint16_t*>(table_shard), T,
                                            shard_rows, static_cast<int>(D), vocab_lo, vocab_total,
-                                           rank, world, epoch, counter, status, err);
+                                           rank, world, state, status, err);
   return check_launch();
 }
 

@@ -240,13 +240,12 @@ class PeerVocabParallelEmbedding:
             raise ValueError("dim must be a multiple of 8")
         self.max_tokens, self.dim = int(max_tokens), int(dim)
         self.device = device or torch.device("cuda", torch.cuda.current_device())
-        # output rows; flags [2][world] int32 at 0 and this rank's counter at 128
+        # output rows; flags [2][world] int32 at 0 and this rank's state words at 128
         self._bufs = _PeerBuffers([self.max_tokens * self.dim * 2, 256], group, self.device)
         self.world, self.rank = self._bufs.world, self._bufs.rank
-        self.epoch = 0
         self._out_arr = self._bufs.array(0)
         self._flag_arr = self._bufs.array(1)
-        self._counter = C.c_void_p(self._bufs.ptrs[1][self.rank] + 128)
+        self._state = C.c_void_p(self._bufs.ptrs[1][self.rank] + 128)  # CTA counter, call count
         self._buf = torch.as_tensor(_DeviceArray(self._bufs.ptrs[0][self.rank], (self.max_tokens, self.dim),
                                                  "<i2"), device=self.device).view(torch.bfloat16)
 
@@ -264,12 +263,11 @@ class PeerVocabParallelEmbedding:
         T = ids_c.numel()
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens > max_tokens {self.max_tokens}")
-        self.epoch += 1
         with torch.cuda.device(self.device):
             st = ops._status_word(self.device)
             _lib.call("frag_embedding_fwd_vp_peer", ops._ptr(ids_c), ops._ptr(table_shard), T,
                       table_shard.shape[0], self.dim, int(vocab_lo), int(vocab_total), self._out_arr,
-                      self._flag_arr, self._counter, self.rank, self.world, self.epoch, ops._ptr(st),
+                      self._flag_arr, self._state, self.rank, self.world, ops._ptr(st),
                       ops._stream(self.device))
         return self._buf[:T].view(*ids.shape, self.dim)
 
@@ -299,9 +297,9 @@ class PeerDweightExchange:
         world, _ = _world(group)
         self._bufs = _PeerBuffers([world * self.n * 4, 256], group, self.device)
         self.world, self.rank = self._bufs.world, self._bufs.rank
-        self.epoch = 0
         self._slots = self._bufs.array(0)
         self._flags = self._bufs.array(1)
+        self._state = C.c_void_p(self._bufs.ptrs[1][self.rank] + 128)  # call count
 
     def __call__(self, dw_local: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         if self._bufs is None:
@@ -311,10 +309,9 @@ class PeerDweightExchange:
             raise ValueError(f"dw_local must be a contiguous fp32 tensor of {self.n} elements")
         out = (torch.empty(self.n, dtype=torch.float32, device=self.device) if out is None
                else ops._check_out(out, "out", torch.float32, self.device, numel=self.n))
-        self.epoch += 1
         with torch.cuda.device(self.device):
             _lib.call("frag_dw_exchange_peer", ops._ptr(dw_local), self.n, self._slots, self._flags,
-                      self.rank, self.world, self.epoch, ops._ptr(out), ops._stream(self.device))
+                      self._state, self.rank, self.world, ops._ptr(out), ops._stream(self.device))
         return out
 
     def close(self) -> None:

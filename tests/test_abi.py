@@ -101,19 +101,18 @@ def test_invalid_arguments_rejected_on_host():
     assert lib.frag_copy_rows_grouped(bad, 1, null) == 2                        # rows overlap
     vp = lib.frag_embedding_fwd_vp_peer
     arr = (C.c_void_p * 8)(*([16] * 8))
-    cnt = C.c_void_p(16)
-    assert vp(null, null, 0, 0, 64, 0, 0, arr, arr, cnt, 0, 0, 1, null, null) == 1    # world 0
-    assert vp(null, null, 0, 0, 64, 0, 0, arr, arr, cnt, 0, 9, 1, null, null) == 1    # > 8 ranks
-    assert vp(null, null, 0, 0, 64, 0, 0, arr, arr, cnt, 2, 2, 1, null, null) == 1    # rank >= world
-    assert vp(null, null, 0, 0, 64, 0, 0, arr, arr, cnt, 0, 2, 0, null, null) == 1    # epoch < 1
-    assert vp(null, null, 0, 0, 64, 0, 0, arr, arr, None, 0, 2, 1, null, null) == 1   # no counter
-    assert vp(null, null, 4, 0, 64, 0, 0, arr, arr, cnt, 0, 2, 1, null, null) == 1    # ids missing
-    assert vp(null, null, 0, 0, 60, 0, 0, arr, arr, cnt, 0, 2, 1, null, null) == 2    # D % 8
+    st = C.c_void_p(16)
+    assert vp(null, null, 0, 0, 64, 0, 0, arr, arr, st, 0, 0, null, null) == 1      # world 0
+    assert vp(null, null, 0, 0, 64, 0, 0, arr, arr, st, 0, 9, null, null) == 1      # > 8 ranks
+    assert vp(null, null, 0, 0, 64, 0, 0, arr, arr, st, 2, 2, null, null) == 1      # rank >= world
+    assert vp(null, null, 0, 0, 64, 0, 0, arr, arr, None, 0, 2, null, null) == 1    # no state
+    assert vp(null, null, 4, 0, 64, 0, 0, arr, arr, st, 0, 2, null, null) == 1      # ids missing
+    assert vp(null, null, 0, 0, 60, 0, 0, arr, arr, st, 0, 2, null, null) == 2      # D % 8
     dx = lib.frag_dw_exchange_peer
-    assert dx(null, 64, arr, arr, 0, 0, 1, null, null) == 1       # world 0
-    assert dx(null, 64, arr, arr, 0, 2, 0, null, null) == 1       # epoch < 1
-    assert dx(null, 64, arr, arr, 0, 2, 1, null, null) == 1       # no vectors
-    assert dx(16, 62, arr, arr, 0, 2, 1, 16, null) == 2           # N % 4
+    assert dx(null, 64, arr, arr, st, 0, 0, null, null) == 1      # world 0
+    assert dx(null, 64, arr, arr, None, 0, 2, null, null) == 1    # no state
+    assert dx(null, 64, arr, arr, st, 0, 2, null, null) == 1      # no vectors
+    assert dx(16, 62, arr, arr, st, 0, 2, 16, null) == 2          # N % 4
     assert lib.frag_peer_alloc(0, None, None) == 1
     assert lib.frag_peer_open(None, None) == 1
     assert lib.frag_peer_close(None) == 1 and lib.frag_peer_free(None) == 1

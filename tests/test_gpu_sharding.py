@@ -87,3 +87,38 @@ def test_peer_dweight_exchange_single_rank():
         ops.check_status(torch.device(DEV))
     finally:
         ex.close()
+
+
+def test_peer_exchanges_replay_from_a_cuda_graph():
+    """Both peer kernels keep their call count on the device, so a captured
+    launch replays correctly (one rank: the flags advance with every replay)."""
+    N = 1024
+    ex = sharding.PeerDweightExchange(N)
+    ec = cf.EmbeddingCfg("peerg", (2, 64), 3000, 256)
+    ids = cf.embedding_ids(ec).to(DEV)
+    table = cf.randn((3000, 256), std=0.02, seed=4).to(DEV)
+    emb = sharding.PeerVocabParallelEmbedding(ids.numel(), 256)
+    try:
+        v = torch.randn(N, device=DEV)
+        out = torch.empty(N, device=DEV)
+        ex(v, out=out)  # first call outside capture
+        holder = {}
+        emb(ids, table, 0, 3000)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ex(v, out=out)
+            holder["y"] = emb(ids, table, 0, 3000)
+        ref = ops.embedding_fwd(ids, table)
+        for k in range(3):
+            v.copy_(torch.randn(N, generator=torch.Generator().manual_seed(k)).to(DEV))
+            out.zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, ops.dw_reduce(v.view(1, N)))
+            assert torch.equal(holder["y"], ref)
+        ops.check_status(torch.device(DEV))
+        del g
+    finally:
+        ex.close()
+        emb.close()
