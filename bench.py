@@ -980,7 +980,20 @@ class L2Flush:
 
 def _time_reps(fn_kernels, fn_after, reps, flush, world):
     """Per rep: flush L2, then events around fn_kernels() and fn_after()
-    (None: nothing).  Returns (mean kernel ms, mean total ms), max over ranks."""
+    (None: nothing).  Returns (mean kernel ms, mean total ms), max over ranks.
+
+    One untimed rep first (a new graph's first replay uploads it), then the
+    ranks line up on the host, so the first timed exchange does not absorb
+    how long each rank took to get here (capturing a graph, for one, takes
+    each rank a different time)."""
+    flush()
+    fn_kernels()
+    if fn_after is not None:
+        fn_after()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
     ka, kb, kc = [], [], []
     for _ in range(reps):
         flush()
@@ -1124,7 +1137,7 @@ def strong_scaling_leg(dev, world, rank, pg, reps=20):
                        "takes its contiguous rows; kernels replayed from a CUDA graph, exchange "
                        "(NCCL all-gather + fixed-order sum) launched eagerly after the replay; *_peer: "
                        "the NVLink peer-memory exchange captured with the kernel in one graph; "
-                       "L2 flushed before each of "
+                       "one untimed rep, ranks lined up on the host, then L2 flushed before each of "
                        f"{reps} reps; efficiency = full-config 1-GPU ms / (N x sharded ms)")}
 
 
@@ -1660,7 +1673,10 @@ def e2e_measure(frags, steps, world, dev, step_bytes):
     global _E2E_PIPE
     hosts = {}
     for f in frags:
-        hosts[f.name] = {"in": {k: v.detach().cpu().pin_memory() for k, v in f.host.items()}, "out": {}}
+        # straight into pinned memory (no pageable copy in between: at 8 ranks
+        # per host the inputs alone are ~95 GB)
+        hosts[f.name] = {"in": {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True).copy_(v.detach())
+                                for k, v in f.host.items()}, "out": {}}
     stream = torch.cuda.current_stream(dev)
     h2d_s = torch.cuda.Stream(dev)
     d2h_s = torch.cuda.Stream(dev)

@@ -168,24 +168,56 @@ class _PeerBuffers:
     rank allocates one buffer per requested size (frag_peer_alloc, zero
     filled), the ranks exchange the IPC handles once (all_gather_object on
     the group) and map every peer's buffers (frag_peer_open).
-    ``ptrs[i][p]`` is rank p's buffer i as seen from this process."""
+    ``ptrs[i][p]`` is rank p's buffer i as seen from this process.
+
+    Construction and ``close()`` are collective and take the same steps on
+    every rank whether or not its own allocation or mapping worked: after the
+    mappings the ranks agree (an all-reduce of an ok flag), so either every
+    rank has all peers mapped before any peer kernel can be launched, or
+    every rank releases what it holds and raises.  ``close()`` unmaps the
+    peers' buffers on every rank before any rank frees its own (freeing an
+    exported buffer that a peer still maps is undefined in CUDA)."""
 
     def __init__(self, sizes: list[int], group, device: torch.device):
         world, rank = _world(group)
         if world > _lib.FRAG_PEER_MAX_RANKS:
             raise ValueError(f"at most {_lib.FRAG_PEER_MAX_RANKS} ranks")
-        self.world, self.rank, self.device = world, rank, device
+        self.world, self.rank, self.device, self.group = world, rank, device, group
         self._own, self._opened = [], []
+        self.ptrs = None
         _lib.load()
+        err = None
         with torch.cuda.device(device):
-            mine = [self._alloc(max(16, int(n))) for n in sizes]
+            mine = []
+            try:
+                mine = [self._alloc(max(16, int(n))) for n in sizes]
+            except Exception as e:  # noqa: BLE001 - reported after the agreement below
+                err = e
             handles = [None] * world
             if world > 1:
-                dist.all_gather_object(handles, [h for _, h in mine], group=group)
+                dist.all_gather_object(handles, None if err else [h for _, h in mine], group=group)
             else:
-                handles[0] = [h for _, h in mine]
-            self.ptrs = [[mine[i][0] if p == rank else self._open(handles[p][i]) for p in range(world)]
-                         for i in range(len(sizes))]
+                handles[0] = None if err else [h for _, h in mine]
+            if err is None and all(h is not None for h in handles):
+                try:
+                    self.ptrs = [[mine[i][0] if p == rank else self._open(handles[p][i])
+                                  for p in range(world)] for i in range(len(sizes))]
+                except Exception as e:  # noqa: BLE001
+                    err = e
+            if not self._agree(err is None and self.ptrs is not None):
+                self.close()
+                raise RuntimeError(
+                    f"peer buffers unavailable on rank {rank}: "
+                    + (repr(err) if err is not None else "another rank could not allocate or map its buffers")
+                ) from err
+
+    def _agree(self, ok: bool) -> bool:
+        """True on every rank iff ``ok`` is true on every rank."""
+        if self.world == 1:
+            return ok
+        t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(t.item())
 
     def _alloc(self, nbytes: int):
         p = C.c_void_p()
@@ -206,14 +238,20 @@ class _PeerBuffers:
         return (C.c_void_p * self.world)(*[q + offset for q in self.ptrs[i]])
 
     def close(self) -> None:
+        """Collective: every rank syncs and unmaps its peers, then (after a
+        barrier) frees its own buffers."""
         lib = _lib.load()
         with torch.cuda.device(self.device):
             torch.cuda.synchronize()
             for p in self._opened:
                 lib.frag_peer_close(C.c_void_p(p))
+            self._opened = []
+            if self.world > 1:
+                dist.barrier(group=self.group)
             for p in self._own:
                 lib.frag_peer_free(C.c_void_p(p))
-        self._own, self._opened = [], []
+            self._own = []
+        self.ptrs = None
 
 
 class PeerVocabParallelEmbedding:

@@ -5,7 +5,9 @@ all-reduce) of the RMSNorm backward and of the forward recomputed in it, the
 vocab-parallel embedding forward (masked gather +
 all-reduce) and backward (per-rank table-gradient shard), and host-side
 failure detection (a rank that raises before a collective, and a rank that
-stalls until the process group's timeout ends the other rank's collective)."""
+stalls until the process group's timeout ends the other rank's collective), and the
+collective setup and teardown of the peer-memory buffers (a rank that cannot
+map its peer makes every rank release its buffers and raise)."""
 import datetime
 import os
 import pickle
@@ -184,6 +186,59 @@ def _body_rank1_stalls(rank):
     return ("completed", time.monotonic() - t0, "")
 
 
+def _peer_buffers_body(fail_rank):
+    """_PeerBuffers with the device calls replaced by fakes: rank `fail_rank`
+    cannot map its peer's buffer (-1: nobody fails)."""
+    import contextlib
+
+    from kernelproblems_b200 import _lib, sharding
+
+    def body(rank):
+        events = []
+
+        class FakeLib:
+            def frag_peer_close(self, p):
+                events.append(("close", p.value))
+                return 0
+
+            def frag_peer_free(self, p):
+                events.append(("free", p.value))
+                return 0
+
+        def fake_alloc(self, n):
+            ptr = 4096 * (rank + 1) + 256 * len(self._own)
+            self._own.append(ptr)
+            return ptr, b"%d" % ptr
+
+        def fake_open(self, h):
+            if rank == fail_rank:
+                raise _lib.FragError("frag_peer_open", 5)
+            self._opened.append(int(h) + 1)
+            return int(h) + 1
+
+        sharding._PeerBuffers._alloc = fake_alloc
+        sharding._PeerBuffers._open = fake_open
+        _lib.load = lambda: FakeLib()
+        torch.cuda.device = lambda d: contextlib.nullcontext()
+        torch.cuda.synchronize = lambda *a, **k: None
+        try:
+            b = sharding._PeerBuffers([64, 256], None, torch.device("cpu"))
+        except RuntimeError as e:
+            return ("raised", str(e)[:200], events)
+        ptrs = [list(row) for row in b.ptrs]
+        b.close()
+        return ("ok", ptrs, events)
+    return body
+
+
+def _peer_ok(rank):
+    return _peer_buffers_body(-1)(rank)
+
+
+def _peer_rank1_fails(rank):
+    return _peer_buffers_body(1)(rank)
+
+
 # ---- tests ------------------------------------------------------------------
 
 @pytest.mark.parametrize("body", [_body_rms, _body_rms_allreduce])
@@ -252,3 +307,28 @@ def test_stalled_rank_ends_collective_by_timeout():
     outcome, elapsed, msg = out[0][1]
     assert outcome == "error", "the waiting rank's collective must fail, not complete"
     assert elapsed < _STALL_S - 1.0, f"error came after {elapsed:.1f}s: the timeout did not end the wait"
+
+
+def test_peer_buffers_map_every_peer_and_free_after_all_unmapped():
+    out = run_ranks(_peer_ok)
+    assert all(st == "ok" for st, _ in out.values()), out
+    for r in range(WORLD):
+        status, ptrs, events = out[r][1]
+        assert status == "ok"
+        own = [4096 * (r + 1), 4096 * (r + 1) + 256]
+        peer = [4096 * (2 - r) + 1, 4096 * (2 - r) + 256 + 1]
+        assert [row[r] for row in ptrs] == own and [row[1 - r] for row in ptrs] == peer
+        # every mapping is closed before this rank frees its own buffers
+        assert events == [("close", q) for q in peer] + [("free", q) for q in own]
+
+
+def test_peer_buffers_fail_together_when_one_rank_cannot_map():
+    out = run_ranks(_peer_rank1_fails)
+    assert all(st == "ok" for st, _ in out.values()), out
+    for r in range(WORLD):
+        status, msg, events = out[r][1]
+        assert status == "raised", "every rank raises, none is left waiting in a peer kernel"
+        assert "peer buffers unavailable" in msg
+        own = [4096 * (r + 1), 4096 * (r + 1) + 256]
+        assert [e for e in events if e[0] == "free"] == [("free", q) for q in own], "own buffers released"
+    assert "another rank" in out[0][1][1] and "frag_peer_open" in out[1][1][1]
