@@ -930,6 +930,27 @@ def _f64_colsum(g, x, r, chunk=8192):
     return s, q
 
 
+def _host_memory_fits(step_bytes, world, dev):
+    """Whether every rank on this host can pin its e2e buffers (about a
+    step's algorithmic bytes of pinned inputs and outputs per rank) within
+    75 % of the host's available memory; all ranks take the same answer."""
+    local = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    avail = 0
+    try:
+        with open("/proc/meminfo") as fh:
+            for ln in fh:
+                if ln.startswith("MemAvailable:"):
+                    avail = int(ln.split()[1]) * 1024
+    except OSError:
+        pass
+    need = step_bytes * local
+    ok = avail == 0 or need < 0.75 * avail  # unknown: assume it fits
+    ok = _all_ok(ok, dev, world)
+    why = (f"{local} ranks x {step_bytes / 1e9:.1f} GB of pinned host buffers would exceed 75% of the "
+           f"{avail / 1e9:.0f} GB available on this host")
+    return ok, ("" if ok else why)
+
+
 def _all_ok(flag: bool, dev, world) -> bool:
     t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=dev)
     if world > 1:
@@ -1647,7 +1668,10 @@ def ours_arm(args, rank, local_rank, world):
             line["triton_reference"] = triton_leg(dev)
 
     # e2e through the public API with host buffers (every step: H2D inputs, D2H outputs)
-    if not args.no_e2e:
+    fits, why = _host_memory_fits(step_bytes, world, dev)
+    if not args.no_e2e and not fits:
+        line["e2e"] = {"value": None, "unit": UNIT, "skipped": why}
+    elif not args.no_e2e:
         line["e2e"] = e2e_measure(frags, args.e2e_steps, world, dev, step_bytes)
         if args.workload == "suite" and args.rows_frac == 1.0 and not args.no_extra:
             line["e2e"]["pcie"] = pcie_leg(dev, world)

@@ -91,6 +91,16 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return v;
 }
 
+// bf16 pair (lo in the low half) <-> fp32 pair, for the f32x2 arithmetic
+// (__fmul2_rn / __ffma2_rn: one instruction for both lanes).
+__device__ __forceinline__ float2 bf16x2_to_f2(uint32_t v) {
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+__device__ __forceinline__ uint32_t f2_to_bf16x2(float2 v) { return pack_bf16x2(v.x, v.y); }
+__device__ __forceinline__ uint32_t u4_word(const uint4& v, int q) {
+  return q == 0 ? v.x : q == 1 ? v.y : q == 2 ? v.z : v.w;
+}
+
 // Streaming 128-bit load: read-only, not kept in L1 (each byte is read once).
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
   uint4 v;
@@ -252,6 +262,22 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, in
 }
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   return mbar_wait_for(bar, parity, err, kWaitCycles);
+}
+// L2 policy "evict first" for data read once: when the L2 must make room,
+// these lines go before others (a clean input line costs no write-back).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// bulk_g2s (below) with an L2 cache policy for the source lines.
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+      "%4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
 }
 // Global -> shared bulk copy of `bytes` (multiple of 16, both addresses
 // 16-byte aligned), completing on `bar`.
