@@ -930,19 +930,21 @@ def _f64_colsum(g, x, r, chunk=8192):
     return s, q
 
 
-def _host_memory_fits(step_bytes, world, dev):
+def _host_memory_fits(step_bytes, world, dev, avail=None):
     """Whether every rank on this host can pin its e2e buffers (about a
     step's algorithmic bytes of pinned inputs and outputs per rank) within
-    75 % of the host's available memory; all ranks take the same answer."""
+    75 % of the host's available memory (`avail` bytes, read from
+    /proc/meminfo when not given); all ranks take the same answer."""
     local = int(os.environ.get("LOCAL_WORLD_SIZE", world))
-    avail = 0
-    try:
-        with open("/proc/meminfo") as fh:
-            for ln in fh:
-                if ln.startswith("MemAvailable:"):
-                    avail = int(ln.split()[1]) * 1024
-    except OSError:
-        pass
+    if avail is None:
+        avail = 0
+        try:
+            with open("/proc/meminfo") as fh:
+                for ln in fh:
+                    if ln.startswith("MemAvailable:"):
+                        avail = int(ln.split()[1]) * 1024
+        except OSError:
+            pass
     need = step_bytes * local
     ok = avail == 0 or need < 0.75 * avail  # unknown: assume it fits
     ok = _all_ok(ok, dev, world)
