@@ -1610,8 +1610,11 @@ def ours_arm(args, rank, local_rank, world):
     tmax = torch.tensor([total_ms] + [statistics.fmean(frag_ms[f.name]) for f in frags]
                         + [statistics.fmean(ex_ms[f.name]) if ex_ms[f.name] else 0.0 for f in frags],
                         dtype=torch.float64, device=dev)
+    tmin = tmax.clone()
     if world > 1:
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tmin, op=dist.ReduceOp.MIN)
+    tmin = tmin.tolist()
     tmax = tmax.tolist()
     ms_step = tmax[0] / K
     value = world * step_bytes / (ms_step * 1e-3) / 1e9
@@ -1660,6 +1663,10 @@ def ours_arm(args, rank, local_rank, world):
             "tokens_per_s_sum_over_fragments": round(world * tokens / (ms_step * 1e-3)),
             "fragments": fr, "roofline": roof, "clocks": clk, "gpu_launches": launches,
             "parity": parity}
+    if world > 1:
+        # the spread of the per-rank figures behind the maxima above
+        line["rank_spread"] = {"ms_per_step_min": round(tmin[0] / K, 4), "ms_per_step_max": round(ms_step, 4),
+                               "fragment_ms_min": {f.name: round(tmin[1 + i], 4) for i, f in enumerate(frags)}}
     step.release()
     if args.workload == "suite" and args.rows_frac == 1.0 and not args.no_extra:
         # the row-sharded configurations at a fixed total (strong scaling), the
