@@ -20,7 +20,10 @@ time per step (CUDA events on the launching stream, CUDA graphs).  At N>1
 every rank runs its own batch (weak scaling); the only collective in the
 step is the dweight exchange of C1B and C4B, which runs on its own stream
 beside the fragments that follow it (C4B's beside the next step's first
-fragments; the per-fragment breakdown times it inline instead).
+fragments; the per-fragment breakdown times it inline instead).  By default
+it is one single-CTA launch over NVLink peer memory (frag_dw_exchange_peer);
+`--exchange nccl` uses the NCCL all-gather + fixed-order sum, which e2e
+always uses (the two give the same bits).
 
 After the timed steps, with the suite's results, the line carries:
   parity            each rank's dweight (C1B, C4B) against the float64 column
@@ -86,6 +89,9 @@ def parse_args(argv=None):
     ap.add_argument("--workload", default="suite",
                     help="suite | next | emb_vp | one fragment of " + ",".join(SUITE + NEXT))
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="dweight exchange of C1B and C4B at N>1 in the timed steps: one launch over "
+                         "NVLink peer memory (default), or NCCL all-gather + fixed-order sum")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the strong-scaling, vocab-parallel and Triton-reference legs")
     ap.add_argument("--e2e-steps", type=int, default=5)
@@ -423,7 +429,7 @@ def scaled_configs(frac: float):
     return rows(cf.C0), rows(cf.C1), c2, c3, rows(cf.C4)
 
 
-def build_suite(dev, world, rank, names, pg, frac=1.0):
+def build_suite(dev, world, rank, names, pg, frac=1.0, exchange="peer"):
     """Build the requested fragments.  Each builder has its own scope, so the
     launch closures never see another fragment's tensors."""
     from kernelproblems_b200 import configs as cf
@@ -432,13 +438,29 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
     C0, C1, C2, C3, C4 = scaled_configs(frac)
 
     def exchange_dw(dw_part, dw_out, parts_buf):
+        """(exchange the step uses, NCCL exchange, peer object or None).  The
+        NCCL exchange all-gathers the per-rank dweights and adds them in rank
+        order; the peer exchange (one single-CTA launch over NVLink peer
+        memory) gives the same bits.  Peer set-up is collective: it either
+        works on every rank or raises on every rank, which then all keep
+        NCCL."""
         if world == 1:
-            return None
+            return None, None, None
 
-        def ex():
+        def ex_nccl():
             dist.all_gather_into_tensor(parts_buf.view(-1), dw_part, group=pg)
             ops.dw_reduce(parts_buf, out=dw_out)
-        return ex
+        if exchange != "peer":
+            return ex_nccl, ex_nccl, None
+        from kernelproblems_b200 import sharding
+        try:
+            peer = sharding.PeerDweightExchange(dw_part.numel(), group=pg, device=dev)
+        except RuntimeError:
+            return ex_nccl, ex_nccl, None
+
+        def ex_peer():
+            peer(dw_part, out=dw_out)
+        return ex_peer, ex_nccl, peer
 
     def mk_c0f():
         c = C0
@@ -465,14 +487,14 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
         dwg = torch.empty(c.N, dtype=torch.float32, device=dev)
         pbuf = torch.empty(world, c.N, dtype=torch.float32, device=dev)
         nb = cf.bytes_add_rmsnorm_bwd(c.M, c.N) if with_dres else cf.bytes_rmsnorm_bwd(c.M, c.N)
+        ex, ex_nccl, peer = exchange_dw(dw, dwg, pbuf)
         if split_stages:
             # row kernel and dweight reduce as two timed stages (the row kernel
             # is the roofline kernel)
             stages = [("rmsnorm_bwd_main", lambda: ops.rmsnorm_bwd(g, x, r, w, dres=dh, dw_dtype=None,
                                                                   workspace=ws)),
                       ("dw_reduce", lambda: ops.dw_reduce(parts, out=dw))]
-            f = Frag(name, c.name + (" bwd" if with_dres else ""), c.M, nb, stages,
-                     exchange=exchange_dw(dw, dwg, pbuf))
+            f = Frag(name, c.name + (" bwd" if with_dres else ""), c.M, nb, stages, exchange=ex)
         else:
             # one call, as a user makes it: row kernel + dependent dweight
             # reduce, into fixed outputs (every captured graph writes the same
@@ -481,7 +503,12 @@ def build_suite(dev, world, rank, names, pg, frac=1.0):
             f = Frag(name, c.name + (" bwd" if with_dres else ""), c.M, nb,
                      [("rmsnorm_bwd", lambda: ops.rmsnorm_bwd(g, x, r, w, dres=dh, workspace=ws,
                                                               dx_out=dx, dw_out=dw))],
-                     exchange=exchange_dw(dw, dwg, pbuf))
+                     exchange=ex)
+        # e2e keeps the NCCL exchange: its steps are host-copy bound, and ranks
+        # can drift further apart there than the peer kernel's bounded waits allow
+        f.exchange_e2e = ex_nccl
+        f.peer = peer
+        f.exchange_kind = None if world == 1 else ("peer" if peer is not None else "nccl")
         f.host = dict(g=g, x=x, r=r) if dh is None else dict(g=g, x=x, r=r, dh=dh)
         f.e2e = lambda h: _e2e_call(lambda xs: ops.rmsnorm_bwd(xs["g"], xs["x"], xs["r"], w,
                                                                dres=xs.get("dh")), h)
@@ -1553,11 +1580,13 @@ def ours_arm(args, rank, local_rank, world):
             print(json.dumps(line), flush=True)
         return 0
     names = {"suite": SUITE, "next": NEXT}.get(args.workload, [args.workload])
-    frags = build_suite(dev, world, rank, names, pg, args.rows_frac)
+    frags = build_suite(dev, world, rank, names, pg, args.rows_frac, exchange=args.exchange)
     step = Step(frags, not args.no_graphs)
     step_bytes = sum(f.bytes for f in frags)
     stream = torch.cuda.current_stream(dev)
 
+    if world > 1:
+        dist.barrier()  # the first exchange's bounded waits start with every rank here
     for _ in range(max(3, args.warmup)):
         step.run()
     step.join()
@@ -1664,6 +1693,7 @@ def ours_arm(args, rank, local_rank, world):
             "fragments": fr, "roofline": roof, "clocks": clk, "gpu_launches": launches,
             "parity": parity}
     if world > 1:
+        line["dweight_exchange"] = {f.name: f.exchange_kind for f in frags if getattr(f, "exchange_kind", None)}
         # the spread of the per-rank figures behind the maxima above
         line["rank_spread"] = {"ms_per_step_min": round(tmin[0] / K, 4), "ms_per_step_max": round(ms_step, 4),
                                "fragment_ms_min": {f.name: round(tmin[1 + i], 4) for i, f in enumerate(frags)}}
@@ -1688,6 +1718,9 @@ def ours_arm(args, rank, local_rank, world):
                 line["e2e"]["dropin"] = e2e_dropin(dev, world)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and set(names) <= set(SUITE):
         line["cpu_baseline"] = cpu_baseline(names, args.cpu_seconds)
+    for f in frags:  # collective: every rank holds the same peer objects
+        if getattr(f, "peer", None) is not None:
+            f.peer.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1718,8 +1751,9 @@ def e2e_measure(frags, steps, world, dev, step_bytes):
         # warm-up (allocator, pinned output buffers)
         for f in frags:
             f.e2e(hosts[f.name])
-            if f.exchange is not None:
-                f.exchange()
+            ex = getattr(f, "exchange_e2e", None) or f.exchange
+            if ex is not None:
+                ex()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -1733,8 +1767,9 @@ def e2e_measure(frags, steps, world, dev, step_bytes):
             h2d = d2h = 0
             for f in frags:
                 i, o = f.e2e(hosts[f.name])
-                if f.exchange is not None:
-                    f.exchange()
+                ex = getattr(f, "exchange_e2e", None) or f.exchange
+                if ex is not None:
+                    ex()
                 h2d += i
                 d2h += o
         stream.wait_stream(h2d_s)  # the end event follows every copy
