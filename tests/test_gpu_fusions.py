@@ -27,6 +27,36 @@ def test_embedding_rmsnorm_fwd(T, V, D, eps):
     assert torch.equal(emb.cpu(), ora.embedding_fwd(table, ids)), "gathered rows bit exact"
 
 
+@pytest.mark.parametrize("T,V,D,save_rstd,emb", [
+    (2000, 5000, 4096, True, False),   # ring: ~5 rows per CTA, rstd only
+    (20000, 50000, 4096, False, True),  # ring: 46 rows per CTA, the 8-stage ring wraps 5 times
+    (460000, 3000, 64, True, True),     # > 1024 rows per CTA: the row-per-CTA kernel instead
+])
+def test_embedding_rmsnorm_fwd_ring_shapes(T, V, D, save_rstd, emb):
+    g = torch.Generator().manual_seed(T)
+    ids = torch.randint(0, V, (T,), generator=g)
+    ids[7] = V + 3  # out of range: a zero row, flagged
+    ids[T // 2] = -1
+    table = cf.randn((V, D), std=0.02, seed=V)
+    w = cf.rmsnorm_weight(D, seed=D + 1)
+    ops.reset_status()
+    y, rstd, e = ops.embedding_rmsnorm_fwd(ids.to(DEV), table.to(DEV), w.to(DEV), 1e-5,
+                                           save_rstd=save_rstd, return_embedding=emb)
+    with pytest.raises(IndexError):
+        ops.check_status()
+    bad = torch.tensor([7, T // 2])
+    assert torch.count_nonzero(y[bad]) == 0
+    keep = torch.ones(T, dtype=torch.bool)
+    keep[bad] = False
+    ey, er = ora.embedding_rmsnorm_fwd(table, ids.clamp(0, V - 1), w, 1e-5)
+    assert_bf16_close(y[keep.to(DEV)], ey[keep], "y")
+    if save_rstd:
+        assert_f32_close(rstd[keep.to(DEV)], er.reshape(-1)[keep], "rstd")
+    if emb:
+        assert torch.count_nonzero(e[bad]) == 0
+        assert torch.equal(e[keep.to(DEV)].cpu(), ora.embedding_fwd(table, ids.clamp(0, V - 1))[keep])
+
+
 def test_embedding_rmsnorm_out_of_range():
     table = cf.randn((16, 64), std=0.02, seed=1).to(DEV)
     w = cf.rmsnorm_weight(64).to(DEV)
